@@ -1,0 +1,142 @@
+"""Parameter layout of face-mlip's FACE model (same state_dict keys and shapes as the reference, so its
+checkpoints load unchanged) and deterministic seeded weights.
+
+Key layout follows face-mlip `face/model.py`:
+  embed (Embedding n_el x C) :570 ; buffers zmap/E0/scale/avg_nb/basis.freq :564-578
+  blocks.t (FactorBlock :421-458 over MomentBlock :99-158)
+     rad_in, pair, radial.{0,2}, msg, mix.{0..3}, proj.{0..3}, elem_scale, pqs_gate, norm, out.{0,2,4},
+     dir_mix/pvt/pmt (pass >= 2), tmix1/2/3 (transport), vpath/mpath/gate (equivariant out)
+  terms.coulomb.head.{0,2} (LatentCharges :80-88)
+"""
+import zlib
+
+import numpy as np
+import torch
+import torch.nn as nn
+
+LINEAR_NAMES = ("rad_in", "radial.0", "radial.2", "msg", "dir_mix", "pvt", "pmt", "tmix1", "tmix2", "tmix3",
+                "gate", "head.0", "head.2") + tuple(f"mix.{l}" for l in range(4)) + tuple(
+    f"proj.{l}" for l in range(4)) + ("out.0", "out.2", "out.4")
+
+
+def _mlp(sizes):
+    layers = []
+    for a, b in zip(sizes[:-1], sizes[1:]):
+        layers += [nn.Linear(a, b), nn.SiLU()]
+    return nn.Sequential(*layers[:-1])
+
+
+class Bessel(nn.Module):
+    def __init__(self, n, rc):
+        super().__init__()
+        self.rc, self.n = rc, n
+        self.register_buffer("freq", torch.arange(1, n + 1) * torch.pi / rc)
+
+
+class Affine(nn.Module):
+    def __init__(self, n):
+        super().__init__()
+        self.w = nn.Parameter(torch.ones(n))
+        self.b = nn.Parameter(torch.zeros(n))
+
+
+class BlockParams(nn.Module):
+    """Parameters of one factorised interaction pass (no compute here; see face_b200.model)."""
+    N_INV = 9
+
+    def __init__(self, C, n_basis, n_sets, radial_hidden, n_el, K_dir, norm, transport, eq_in, eq_out, B, K):
+        super().__init__()
+        self.C, self.B, self.Km, self.Kd, self.n_el = C, B, K, K_dir, n_el
+        self.eq_in, self.eq_out = eq_in, eq_out
+        self.directional = n_sets > 1
+        self.transport = transport and self.directional
+        self.pqs_gate = nn.Embedding(n_el, 12 * C)
+        self.register_buffer("mom_scale", torch.ones(4))
+        self.register_buffer("eq_scale", torch.ones(2))
+        self.register_buffer("inv_scale", torch.ones(self.N_INV))
+        self.register_buffer("calibrated", torch.tensor(False))
+        self.rad_in = nn.Linear(n_basis, radial_hidden)
+        self.pair = nn.Embedding(n_el * n_el, radial_hidden)
+        cin = C * n_sets
+        self.proj = nn.ModuleList([nn.Linear(cin, 3 * C, bias=False) for _ in range(4)])
+        self.elem_scale = nn.Embedding(n_el, 4 * C)
+        self.out = _mlp([self.N_INV * C + C + 4, 2 * C, 2 * C, C + 1])
+        self.norm_kind = norm
+        if norm == "layer":
+            self.norm = nn.LayerNorm(self.N_INV * C)
+        elif norm == "affine":
+            self.norm = Affine(self.N_INV * C)
+        else:
+            self.norm = nn.Identity()
+        if eq_out:
+            self.vpath = nn.Parameter(torch.ones(4, C))
+            self.mpath = nn.Parameter(torch.ones(4, C))
+            self.gate = nn.Linear(self.N_INV * C, 2 * C)
+        self.radial = _mlp([radial_hidden, radial_hidden, B])
+        self.msg = nn.Linear(C, K)
+        self.mix = nn.ModuleList([nn.Linear(B * K, C, bias=False) for _ in range(4)])
+        if self.directional:
+            self.dir_mix = nn.Linear(4 * K_dir, K)
+            cprev = C if eq_in else C * (n_sets - 1)
+            nt = 2 if self.transport else 1
+            self.pvt = nn.Linear(cprev, nt * K_dir, bias=False)
+            self.pmt = nn.Linear(cprev, nt * K_dir, bias=False)
+        if self.transport:
+            self.tmix1 = nn.Linear(B * 2 * K_dir, C, bias=False)
+            self.tmix2 = nn.Linear(B * 2 * K_dir, C, bias=False)
+            self.tmix3 = nn.Linear(B * 2 * K_dir, C, bias=False)
+
+
+class ChargeParams(nn.Module):
+    """LatentCharges parameters (face/electrostatics.py:81-88)."""
+
+    def __init__(self, C, sigma=0.5, rc_real=5.0, acc=3.5):
+        super().__init__()
+        self.head = nn.Sequential(nn.Linear(C, C), nn.SiLU(), nn.Linear(C, 2))
+        self.sigma, self.gamma = sigma, 2 * sigma
+        self.gp = max(rc_real / acc, 1.05 * self.gamma)
+        self.kcut = 2 * acc / self.gp
+        self.mesh = None            # None -> face-mlip's rule n = max(8, ceil(L / (gp/4)))
+
+
+def _fan_in(model, name):
+    return model.get_parameter(name.rsplit(".", 1)[0] + ".weight").shape[1]
+
+
+def seeded_state(model, seed, perturb=0.25):
+    """Deterministic random weights: each parameter from its own stream keyed by (seed, crc32(name)), with the
+    reference's initial distribution (nn.Linear uniform(+-1/sqrt(fan_in)) -- stored as uniform(+-1) under unit
+    parameterisation --, embeddings N(0,1), ones/zeros where the reference initialises them so), then every
+    stored parameter gets + perturb * N(0,1) as in face-mlip tests/test_symmetry.py:32-33.  Without the
+    perturbation a random-init model gives forces of ~1e-3 eV/A; with 0.25 the 5-element alloy model gives
+    force rms ~0.5 eV/A and charge rms ~0.3 e (physical magnitudes)."""
+    out = {}
+    unit = getattr(model, "unit", False)
+    for name, p in model.named_parameters():
+        rng = np.random.default_rng([seed, zlib.crc32(name.encode())])
+        amp = perturb
+        sh = tuple(p.shape)
+        mod, leaf = name.rsplit(".", 1)
+        last = mod.split(".")[-1]
+        two = ".".join(mod.split(".")[-2:])
+        is_lin = last in LINEAR_NAMES or two in LINEAR_NAMES
+        if last == "gate":                                  # face/model.py:158
+            base = np.zeros(sh) if leaf == "weight" else np.ones(sh)
+        elif is_lin and leaf == "weight":
+            bound = 1.0 if unit else _fan_in(model, name) ** -0.5
+            base = rng.uniform(-bound, bound, sh)
+        elif is_lin and leaf == "bias":
+            bound = _fan_in(model, name) ** -0.5
+            base = rng.uniform(-bound, bound, sh)
+        elif last == "pair":                                # face/model.py:128
+            base = np.zeros(sh)
+        elif last in ("elem_scale", "pqs_gate") or leaf in ("vpath", "mpath") or (last == "norm" and leaf in ("weight", "w")):
+            base = np.ones(sh)
+        elif last == "norm":
+            base = np.zeros(sh)
+        else:                                               # embed.weight
+            base = rng.standard_normal(sh)
+        # rounded to float32 so that float32 and float64 models hold identical values
+        val = (base + amp * rng.standard_normal(sh)).astype(np.float32).astype(np.float64)
+        out[name] = torch.as_tensor(val, dtype=p.dtype)
+    return out
