@@ -1,0 +1,840 @@
+// Edge-level kernels of the FACE engine (face-mlip face/model.py:665-679, :460-534):
+//   edge vectors and the force gather, symmetric monomials Y(u), the radial basis x radial MLP with
+//   forward-mode dphi/dr (or the cubic Hermite spline), directional edge messages, transport sums.
+// All scatter-to-neighbour adjoints use the reverse-edge index of the symmetric neighbour list (gathers,
+// no atomics, deterministic).
+#include "common.cuh"
+
+namespace facek {
+namespace {
+
+constexpr int NX = 20;
+
+template <typename T>
+__device__ __forceinline__ T sigmoid(T z) {
+  return T(1) / (T(1) + exp(-z));
+}
+
+// ------------------------------------------------------------------------------------------ geometry
+template <typename T>
+__global__ void edge_vec_k(const T* __restrict__ pos, const int32_t* __restrict__ ei, const int32_t* __restrict__ ej,
+                           const T* __restrict__ shift, T* __restrict__ vec, int64_t E) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < E; e += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t i = ei[e], j = ej[e];
+#pragma unroll
+    for (int d = 0; d < 3; d++) vec[e * 3 + d] = (pos[j * 3 + d] - pos[i * 3 + d]) + shift[e * 3 + d];
+  }
+}
+
+// dpos[k] = sum_{e in row k} (dvec[rev e] - dvec[e])
+template <typename T>
+__global__ void edge_vec_bwd_k(const T* __restrict__ dvec, const int32_t* __restrict__ row_ptr,
+                               const int32_t* __restrict__ rev, int64_t N, T* __restrict__ dpos) {
+  for (int64_t k = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; k < N; k += (int64_t)gridDim.x * blockDim.x) {
+    T g0 = 0, g1 = 0, g2 = 0;
+    for (int e = row_ptr[k]; e < row_ptr[k + 1]; e++) {
+      const int64_t r = rev[e];
+      g0 += dvec[r * 3 + 0] - dvec[(int64_t)e * 3 + 0];
+      g1 += dvec[r * 3 + 1] - dvec[(int64_t)e * 3 + 1];
+      g2 += dvec[r * 3 + 2] - dvec[(int64_t)e * 3 + 2];
+    }
+    dpos[k * 3 + 0] = g0;
+    dpos[k * 3 + 1] = g1;
+    dpos[k * 3 + 2] = g2;
+  }
+}
+
+template <typename T>
+__device__ __forceinline__ void monomials(T x, T y, T z, T* Y) {
+  Y[0] = T(1); Y[1] = x; Y[2] = y; Y[3] = z;
+  Y[4] = x * x; Y[5] = y * y; Y[6] = z * z; Y[7] = x * y; Y[8] = x * z; Y[9] = y * z;
+  Y[10] = x * x * x; Y[11] = y * y * y; Y[12] = z * z * z; Y[13] = x * x * y; Y[14] = x * x * z;
+  Y[15] = x * y * y; Y[16] = y * y * z; Y[17] = x * z * z; Y[18] = y * z * z; Y[19] = x * y * z;
+}
+
+// gradient of the 20 monomials w.r.t. u
+template <typename T>
+__device__ __forceinline__ void monomials_bwd(T x, T y, T z, const T* g, T& ux, T& uy, T& uz) {
+  ux = g[1] + 2 * x * g[4] + y * g[7] + z * g[8] + 3 * x * x * g[10] + 2 * x * y * g[13] + 2 * x * z * g[14] +
+       y * y * g[15] + z * z * g[17] + y * z * g[19];
+  uy = g[2] + 2 * y * g[5] + x * g[7] + z * g[9] + 3 * y * y * g[11] + x * x * g[13] + 2 * x * y * g[15] +
+       2 * y * z * g[16] + z * z * g[18] + x * z * g[19];
+  uz = g[3] + 2 * z * g[6] + x * g[8] + y * g[9] + 3 * z * z * g[12] + x * x * g[14] + y * y * g[16] +
+       2 * x * z * g[17] + 2 * y * z * g[18] + x * y * g[19];
+}
+
+// du -> dvec for u = vec / |vec|
+template <typename T>
+__device__ __forceinline__ void unit_bwd(T ux, T uy, T uz, T r, T gx, T gy, T gz, T& dx, T& dy, T& dz) {
+  const T ud = ux * gx + uy * gy + uz * gz;
+  dx = (gx - ux * ud) / r;
+  dy = (gy - uy * ud) / r;
+  dz = (gz - uz * ud) / r;
+}
+
+template <typename T>
+__global__ void edge_sym_k(const T* __restrict__ vec, T* __restrict__ Y, int64_t E) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < E; e += (int64_t)gridDim.x * blockDim.x) {
+    const T vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+    const T r = sqrt(vx * vx + vy * vy + vz * vz);
+    T y[NX];
+    monomials(vx / r, vy / r, vz / r, y);
+#pragma unroll
+    for (int x = 0; x < NX; x++) Y[e * NX + x] = y[x];
+  }
+}
+
+template <typename T>
+__global__ void edge_sym_bwd_k(const T* __restrict__ vec, const T* __restrict__ dY, T* __restrict__ dvec, int acc,
+                               int64_t E) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < E; e += (int64_t)gridDim.x * blockDim.x) {
+    const T vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+    const T r = sqrt(vx * vx + vy * vy + vz * vz);
+    const T ux = vx / r, uy = vy / r, uz = vz / r;
+    T g[NX];
+#pragma unroll
+    for (int x = 0; x < NX; x++) g[x] = dY[e * NX + x];
+    T gx, gy, gz, dx, dy, dz;
+    monomials_bwd(ux, uy, uz, g, gx, gy, gz);
+    unit_bwd(ux, uy, uz, r, gx, gy, gz, dx, dy, dz);
+    if (acc) {
+      dvec[e * 3] += dx; dvec[e * 3 + 1] += dy; dvec[e * 3 + 2] += dz;
+    } else {
+      dvec[e * 3] = dx; dvec[e * 3 + 1] = dy; dvec[e * 3 + 2] = dz;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------ radial
+// polynomial envelope p = 6 (face/model.py:34-37) and its r-derivative
+template <typename T>
+__device__ __forceinline__ void envelope(T r, T rc, T& env, T& denv) {
+  const T x = r / rc;
+  if (x >= T(1)) {
+    env = 0;
+    denv = 0;
+    return;
+  }
+  const T x2 = x * x, x5 = x2 * x2 * x, x6 = x5 * x, x7 = x6 * x, x8 = x7 * x;
+  env = T(1) - T(28) * x6 + T(48) * x7 - T(21) * x8;
+  denv = (T(-168) * x5 + T(336) * x6 - T(168) * x7) / rc;
+}
+
+template <typename T, int NBMAX, int HMAX, int BMAX>
+__global__ void __launch_bounds__(128) radial_mlp_k(const T* __restrict__ vec, const int32_t* __restrict__ ei,
+                                                    const int32_t* __restrict__ ej, const int32_t* __restrict__ zidx,
+                                                    int n_el, T rc, int nb, int H, int B, const T* __restrict__ w1,
+                                                    const T* __restrict__ b1, const T* __restrict__ pair,
+                                                    const T* __restrict__ w2, const T* __restrict__ b2,
+                                                    const T* __restrict__ w3, const T* __restrict__ b3,
+                                                    T* __restrict__ phi, T* __restrict__ dphidr, int64_t E) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* sW1 = reinterpret_cast<T*>(smem_raw);   // H x nb
+  T* sB1 = sW1 + H * nb;                      // H
+  T* sPair = sB1 + H;                         // n_el^2 x H
+  T* sW2 = sPair + n_el * n_el * H;           // H x H
+  T* sB2 = sW2 + H * H;                       // H
+  T* sW3 = sB2 + H;                           // B x H
+  T* sB3 = sW3 + B * H;                       // B
+  for (int q = threadIdx.x; q < H * nb; q += blockDim.x) sW1[q] = w1[q];
+  for (int q = threadIdx.x; q < H; q += blockDim.x) { sB1[q] = b1[q]; sB2[q] = b2[q]; }
+  for (int q = threadIdx.x; q < n_el * n_el * H; q += blockDim.x) sPair[q] = pair[q];
+  for (int q = threadIdx.x; q < H * H; q += blockDim.x) sW2[q] = w2[q];
+  for (int q = threadIdx.x; q < B * H; q += blockDim.x) sW3[q] = w3[q];
+  for (int q = threadIdx.x; q < B; q += blockDim.x) sB3[q] = b3[q];
+  __syncthreads();
+  const T c = sqrt(T(2) / rc);
+  const T pi = T(3.14159265358979323846);
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < E; e += (int64_t)gridDim.x * blockDim.x) {
+    const T vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+    const T r = sqrt(vx * vx + vy * vy + vz * vz);
+    T env, denv;
+    envelope(r, rc, env, denv);
+    T rb[NBMAX], drb[NBMAX];
+#pragma unroll
+    for (int n = 0; n < NBMAX; n++) {
+      if (n < nb) {
+        const T f = T(n + 1) * pi / rc;
+        T s, co;
+        s = sin(f * r);
+        co = cos(f * r);
+        const T bes = s / r * c;
+        const T dbes = (f * co / r - s / (r * r)) * c;
+        rb[n] = bes * env;
+        drb[n] = dbes * env + bes * denv;
+      } else {
+        rb[n] = 0;
+        drb[n] = 0;
+      }
+    }
+    const T* prow = sPair + (zidx[ei[e]] * n_el + zidx[ej[e]]) * H;
+    T a1[HMAX], da1[HMAX];
+#pragma unroll
+    for (int h = 0; h < HMAX; h++) {
+      if (h < H) {
+        T z = sB1[h] + prow[h], dz = 0;
+#pragma unroll
+        for (int n = 0; n < NBMAX; n++)
+          if (n < nb) {
+            z += sW1[h * nb + n] * rb[n];
+            dz += sW1[h * nb + n] * drb[n];
+          }
+        const T s = sigmoid(z);
+        a1[h] = z * s;
+        da1[h] = s * (T(1) + z * (T(1) - s)) * dz;
+      } else {
+        a1[h] = 0;
+        da1[h] = 0;
+      }
+    }
+    T z3[BMAX], dz3[BMAX];
+#pragma unroll
+    for (int b = 0; b < BMAX; b++) { z3[b] = 0; dz3[b] = 0; }
+    for (int o = 0; o < H; o++) {
+      const T* w = sW2 + o * H;
+      T z = sB2[o], dz = 0;
+#pragma unroll
+      for (int h = 0; h < HMAX; h++)
+        if (h < H) {
+          z += w[h] * a1[h];
+          dz += w[h] * da1[h];
+        }
+      const T s = sigmoid(z);
+      const T a2 = z * s, da2 = s * (T(1) + z * (T(1) - s)) * dz;
+#pragma unroll
+      for (int b = 0; b < BMAX; b++)
+        if (b < B) {
+          z3[b] += sW3[b * H + o] * a2;
+          dz3[b] += sW3[b * H + o] * da2;
+        }
+    }
+#pragma unroll
+    for (int b = 0; b < BMAX; b++)
+      if (b < B) {
+        const T v = z3[b] + sB3[b];
+        phi[e * B + b] = v * env;
+        dphidr[e * B + b] = dz3[b] * env + v * denv;
+      }
+  }
+}
+
+template <typename T, int BMAX>
+__global__ void radial_spline_k(const T* __restrict__ vec, const int32_t* __restrict__ ei,
+                                const int32_t* __restrict__ ej, const int32_t* __restrict__ zidx, int n_el, T rc,
+                                int G, T dr, int B, const T* __restrict__ Tab, const T* __restrict__ dTab,
+                                T* __restrict__ phi, T* __restrict__ dphidr, int64_t E) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < E; e += (int64_t)gridDim.x * blockDim.x) {
+    const T vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+    const T r = sqrt(vx * vx + vy * vy + vz * vz);
+    T env, denv;
+    envelope(r, rc, env, denv);
+    T x = r / dr;
+    T dxdr = T(1) / dr;
+    if (x < T(0)) { x = 0; dxdr = 0; }
+    if (x > T(G - 1)) { x = T(G - 1); dxdr = 0; }
+    int i = (int)floor(x);
+    if (i > G - 2) i = G - 2;
+    const T t = x - T(i), t2 = t * t, t3 = t2 * t;
+    const T h00 = 2 * t3 - 3 * t2 + 1, h10 = t3 - 2 * t2 + t, h01 = -2 * t3 + 3 * t2, h11 = t3 - t2;
+    const T g00 = 6 * t2 - 6 * t, g10 = 3 * t2 - 4 * t + 1, g01 = -6 * t2 + 6 * t, g11 = 3 * t2 - 2 * t;
+    const int64_t base = ((int64_t)(zidx[ei[e]] * n_el + zidx[ej[e]]) * G + i) * B;
+    for (int b = 0; b < B; b++) {
+      const T p0 = Tab[base + b], p1 = Tab[base + B + b];
+      const T m0 = dTab[base + b] * dr, m1 = dTab[base + B + b] * dr;
+      const T v = h00 * p0 + h10 * m0 + h01 * p1 + h11 * m1;
+      const T dv = (g00 * p0 + g10 * m0 + g01 * p1 + g11 * m1) * dxdr;
+      phi[e * B + b] = v * env;
+      dphidr[e * B + b] = dv * env + v * denv;
+    }
+  }
+}
+
+template <typename T>
+__global__ void radial_bwd_k(const T* __restrict__ vec, const T* __restrict__ dphi, const T* __restrict__ dphidr,
+                             int B, T* __restrict__ dvec, int acc, int64_t E) {
+  for (int64_t e = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; e < E; e += (int64_t)gridDim.x * blockDim.x) {
+    const T vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+    const T r = sqrt(vx * vx + vy * vy + vz * vz);
+    T s = 0;
+    for (int b = 0; b < B; b++) s += dphi[e * B + b] * dphidr[e * B + b];
+    const T gx = s * vx / r, gy = s * vy / r, gz = s * vz / r;
+    if (acc) {
+      dvec[e * 3] += gx; dvec[e * 3 + 1] += gy; dvec[e * 3 + 2] += gz;
+    } else {
+      dvec[e * 3] = gx; dvec[e * 3 + 1] = gy; dvec[e * 3 + 2] = gz;
+    }
+  }
+}
+
+// ------------------------------------------------------------------------------------------ messages
+template <typename T>
+__global__ void edge_msg_k(const T* __restrict__ Y, const int32_t* __restrict__ ei, const int32_t* __restrict__ ej,
+                           const T* __restrict__ TJ, const T* __restrict__ TI, int nc, int K, int64_t N,
+                           T* __restrict__ msg, int64_t EK) {
+  const int64_t NK = N * K;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < EK; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = q / K;
+    const int k = (int)(q - e * K);
+    const T* tj = TJ + (int64_t)ej[e] * K + k;
+    T s = 0;
+    if (TI) {
+      const T* ti = TI + (int64_t)ei[e] * K + k;
+      for (int c = 0; c < nc; c++) s += Y[e * NX + c] * (tj[c * NK] + ti[c * NK]);
+    } else {
+      for (int c = 0; c < nc; c++) s += Y[e * NX + c] * tj[c * NK];
+    }
+    msg[q] = s;
+  }
+}
+
+// dY[e, c<nc] (+)= sum_k dmsg[e,k] (TJ[ej,c,k] + TI[ei,c,k]); one warp per edge
+template <typename T>
+__global__ void edge_msg_bwd_dy_k(const int32_t* __restrict__ ei, const int32_t* __restrict__ ej,
+                                  const T* __restrict__ TJ, const T* __restrict__ TI, const T* __restrict__ dmsg,
+                                  int nc, int K, int64_t N, T* __restrict__ dY, int acc, int64_t E) {
+  const int64_t NK = N * K;
+  const int lane = threadIdx.x & 31;
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+  for (int64_t e = blockIdx.x * (int64_t)(blockDim.x >> 5) + (threadIdx.x >> 5); e < E; e += warps) {
+    T part[10];
+#pragma unroll
+    for (int c = 0; c < 10; c++) part[c] = 0;
+    const T* tj = TJ + (int64_t)ej[e] * K;
+    const T* ti = TI ? TI + (int64_t)ei[e] * K : nullptr;
+    for (int k = lane; k < K; k += 32) {
+      const T g = dmsg[e * K + k];
+#pragma unroll
+      for (int c = 0; c < 10; c++)
+        if (c < nc) part[c] += g * (tj[c * NK + k] + (ti ? ti[c * NK + k] : T(0)));
+    }
+#pragma unroll
+    for (int c = 0; c < 10; c++) {
+      T v = part[c];
+      for (int off = 16; off > 0; off >>= 1) v += __shfl_xor_sync(0xffffffffu, v, off);
+      part[c] = v;
+    }
+    if (lane < nc) {
+      T v = 0;
+#pragma unroll
+      for (int c = 0; c < 10; c++)
+        if (c == lane) v = part[c];
+      if (acc)
+        dY[e * NX + lane] += v;
+      else
+        dY[e * NX + lane] = v;
+    }
+    if (!acc && lane >= nc && lane < NX) dY[e * NX + lane] = 0;
+  }
+}
+
+// dTJ[c,a,k] = sum_{e in row a} Y[rev e, c] dmsg[rev e, k];  dTI[c,a,k] = sum_{e in row a} Y[e, c] dmsg[e, k]
+template <typename T>
+__global__ void edge_msg_bwd_tables_k(const T* __restrict__ Y, const T* __restrict__ dmsg,
+                                      const int32_t* __restrict__ row_ptr, const int32_t* __restrict__ rev, int nc,
+                                      int K, T* __restrict__ dTJ, T* __restrict__ dTI, int64_t NK) {
+  // q = a*K + k indexes (atom, channel); plane c of a (nc, N, K) table starts at c*NK
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < NK; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t a = q / K;
+    const int k = (int)(q - a * K);
+    T sj[10], si[10];
+#pragma unroll
+    for (int c = 0; c < 10; c++) { sj[c] = 0; si[c] = 0; }
+    for (int e = row_ptr[a]; e < row_ptr[a + 1]; e++) {
+      const int64_t r = rev[e];
+      const T gr = dmsg[r * K + k];
+      const T ge = dmsg[(int64_t)e * K + k];
+#pragma unroll
+      for (int c = 0; c < 10; c++)
+        if (c < nc) {
+          sj[c] += Y[r * NX + c] * gr;
+          si[c] += Y[(int64_t)e * NX + c] * ge;
+        }
+    }
+#pragma unroll
+    for (int c = 0; c < 10; c++)
+      if (c < nc) {
+        dTJ[c * NK + q] = sj[c];
+        if (dTI) dTI[c * NK + q] = si[c];
+      }
+  }
+}
+
+// ------------------------------------------------------------------------------------------ transport
+// storage row of transport output o (see facek.h): V_a -> 2a, (M u)_a -> 2a+1, M_s -> 6+2s, sym(uV)_s -> 7+2s
+__host__ __device__ constexpr int trow(int o) {
+  return o < 3 ? 2 * o : (o < 6 ? 2 * (o - 3) + 1 : (o < 12 ? 6 + 2 * (o - 6) : 7 + 2 * (o - 12)));
+}
+__host__ __device__ constexpr int s2i(int a, int b) { return a == b ? a : 2 + a + b; }
+__host__ __device__ constexpr int pair_p(int s) { return s < 3 ? s : (s == 5 ? 1 : 0); }
+__host__ __device__ constexpr int pair_q(int s) { return s < 3 ? s : (s == 3 ? 1 : 2); }
+
+template <typename T>
+__device__ __forceinline__ void transport_f(T ux, T uy, T uz, const T g[9], T f[18]) {
+  const T u[3] = {ux, uy, uz};
+#pragma unroll
+  for (int a = 0; a < 3; a++) f[a] = g[a];
+#pragma unroll
+  for (int a = 0; a < 3; a++) {
+    T s = 0;
+#pragma unroll
+    for (int b = 0; b < 3; b++) s += g[3 + s2i(a, b)] * u[b];
+    f[3 + a] = s;
+  }
+#pragma unroll
+  for (int s = 0; s < 6; s++) f[6 + s] = g[3 + s];
+#pragma unroll
+  for (int s = 0; s < 6; s++) {
+    const int p = pair_p(s), q = pair_q(s);
+    f[12 + s] = p == q ? u[p] * g[p] : T(0.5) * (u[p] * g[q] + u[q] * g[p]);
+  }
+}
+
+constexpr int TR_TILE = 16;
+
+// storage row r (= trow(o)) of atom i in the two transport planes, as one offset from the start of plane 1:
+// plane 1 (3, N, 2, BKd) holds rows 0..5 as (comp r/2, t r%2); plane 2 (6, N, 2, BKd) rows 6..17 likewise
+__host__ __device__ inline int64_t plane_off(int r, int64_t i, int64_t N, int BKd) {
+  if (r < 6) return (((int64_t)(r >> 1) * N + i) * 2 + (r & 1)) * BKd;
+  const int s = r - 6;
+  return 6 * N * (int64_t)BKd + (((int64_t)(s >> 1) * N + i) * 2 + (s & 1)) * BKd;
+}
+
+// CTA per row; thread (b-quad, kd) accumulates 4 x 18 outputs; edges staged in shared memory
+template <typename T>
+__global__ void __launch_bounds__(256) transport_fwd_k(const T* __restrict__ phi, const T* __restrict__ vec,
+                                                       const int32_t* __restrict__ ej, const T* __restrict__ Gt,
+                                                       const int32_t* __restrict__ row_ptr, T* __restrict__ DT,
+                                                       int64_t N, int B, int Kd) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* sP = reinterpret_cast<T*>(smem_raw);   // TR_TILE x B
+  T* sF = sP + TR_TILE * B;                  // TR_TILE x Kd x 18
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int nbq = B / 4;
+  const int kd = tid % Kd, bq = tid / Kd;
+  const bool active = bq < nbq;
+  const int BKd = B * Kd;
+  for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
+    const int64_t e0 = row_ptr[i];
+    const int deg = row_ptr[i + 1] - row_ptr[i];
+    T acc[4][18];
+#pragma unroll
+    for (int a = 0; a < 4; a++)
+#pragma unroll
+      for (int o = 0; o < 18; o++) acc[a][o] = 0;
+    for (int t0 = 0; t0 < deg; t0 += TR_TILE) {
+      const int nt = min(TR_TILE, deg - t0);
+      __syncthreads();
+      for (int q = tid; q < nt * B; q += nthr) sP[q] = phi[(e0 + t0) * B + q];
+      for (int q = tid; q < nt * Kd; q += nthr) {
+        const int t = q / Kd, k = q - t * Kd;
+        const int64_t e = e0 + t0 + t;
+        const T vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+        const T r = sqrt(vx * vx + vy * vy + vz * vz);
+        const T* gj = Gt + (int64_t)ej[e] * Kd + k;
+        T g[9], f[18];
+#pragma unroll
+        for (int c = 0; c < 9; c++) g[c] = gj[c * N * Kd];
+        transport_f(vx / r, vy / r, vz / r, g, f);
+#pragma unroll
+        for (int o = 0; o < 18; o++) sF[(t * Kd + k) * 18 + o] = f[o];
+      }
+      __syncthreads();
+      if (active) {
+        for (int t = 0; t < nt; t++) {
+          T f[18];
+#pragma unroll
+          for (int o = 0; o < 18; o++) f[o] = sF[(t * Kd + kd) * 18 + o];
+#pragma unroll
+          for (int a = 0; a < 4; a++) {
+            const T p = sP[t * B + bq * 4 + a];
+#pragma unroll
+            for (int o = 0; o < 18; o++) acc[a][o] += p * f[o];
+          }
+        }
+      }
+    }
+    if (active) {
+#pragma unroll
+      for (int o = 0; o < 18; o++) {
+        T* out = DT + plane_off(trow(o), i, N, BKd);
+#pragma unroll
+        for (int a = 0; a < 4; a++) out[(bq * 4 + a) * Kd + kd] = acc[a][o];
+      }
+    }
+  }
+}
+
+// CTA per row with dDT staged in shared memory; each edge handled by Kd/4 threads (4 kd channels each)
+template <typename T, int BMAX>
+__global__ void __launch_bounds__(128) transport_bwd_k(const T* __restrict__ phi, const T* __restrict__ vec,
+                                                       const int32_t* __restrict__ ej, const T* __restrict__ Gt,
+                                                       const T* __restrict__ dT1, const T* __restrict__ dT2,
+                                                       const int32_t* __restrict__ row_ptr,
+                                                       T* __restrict__ dphi, T* __restrict__ dvec, int acc,
+                                                       T* __restrict__ dGe, int64_t N, int B, int Kd, int KQ) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* sD = reinterpret_cast<T*>(smem_raw);   // 18 x B*Kd
+  const int tid = threadIdx.x, nthr = blockDim.x;
+  const int BKd = B * Kd;
+  const int kq = tid % KQ, slot = tid / KQ, per_pass = nthr / KQ;
+  for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
+    const int64_t e0 = row_ptr[i];
+    const int deg = row_ptr[i + 1] - row_ptr[i];
+    __syncthreads();
+    for (int q = tid; q < 18 * BKd; q += nthr) {
+      const int r = q / BKd, c = q - r * BKd;
+      const int64_t off = plane_off(r, i, N, BKd);
+      sD[q] = r < 6 ? dT1[off + c] : dT2[off - 6 * N * (int64_t)BKd + c];
+    }
+    __syncthreads();
+    for (int t0 = 0; t0 < deg; t0 += per_pass) {
+      const int t = t0 + slot;
+      const bool live = t < deg;
+      const int64_t e = e0 + (live ? t : 0);
+      const T vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+      const T r = sqrt(vx * vx + vy * vy + vz * vz);
+      const T u[3] = {vx / r, vy / r, vz / r};
+      T p[BMAX], dp[BMAX];
+#pragma unroll
+      for (int b = 0; b < BMAX; b++) { p[b] = (live && b < B) ? phi[e * B + b] : T(0); dp[b] = 0; }
+      T g[4][9], f[4][18], Pd[4][18];
+      const T* gj = Gt + (int64_t)ej[e] * Kd;
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        const int k = kq * 4 + q;
+#pragma unroll
+        for (int c = 0; c < 9; c++) g[q][c] = k < Kd ? gj[c * N * Kd + k] : T(0);
+        transport_f(u[0], u[1], u[2], g[q], f[q]);
+#pragma unroll
+        for (int o = 0; o < 18; o++) Pd[q][o] = 0;
+      }
+#pragma unroll
+      for (int o = 0; o < 18; o++) {
+        const T* row = sD + (int64_t)trow(o) * BKd + kq * 4;
+#pragma unroll
+        for (int b = 0; b < BMAX; b++) {
+          if (b < B) {
+            T d4[4];
+#pragma unroll
+            for (int q = 0; q < 4; q++) d4[q] = (kq * 4 + q < Kd) ? row[b * Kd + q] : T(0);
+#pragma unroll
+            for (int q = 0; q < 4; q++) {
+              Pd[q][o] += p[b] * d4[q];
+              dp[b] += d4[q] * f[q][o];
+            }
+          }
+        }
+      }
+      // dphi: reduce over the KQ threads of this edge
+      for (int off = 1; off < KQ; off <<= 1)
+#pragma unroll
+        for (int b = 0; b < BMAX; b++) dp[b] += __shfl_xor_sync(0xffffffffu, dp[b], off);
+      // adjoint of f -> dV, dMs (per kd) and du
+      T du[3] = {0, 0, 0};
+#pragma unroll
+      for (int q = 0; q < 4; q++) {
+        T dV[3], dM[6];
+#pragma unroll
+        for (int a = 0; a < 3; a++) dV[a] = Pd[q][a];
+#pragma unroll
+        for (int s = 0; s < 6; s++) dM[s] = Pd[q][6 + s];
+#pragma unroll
+        for (int a = 0; a < 3; a++)
+#pragma unroll
+          for (int b = 0; b < 3; b++) {
+            dM[s2i(a, b)] += Pd[q][3 + a] * u[b];
+            du[b] += Pd[q][3 + a] * g[q][3 + s2i(a, b)];
+          }
+#pragma unroll
+        for (int s = 0; s < 6; s++) {
+          const int pp = pair_p(s), qq = pair_q(s);
+          const T w = Pd[q][12 + s];
+          if (pp == qq) {
+            du[pp] += w * g[q][pp];
+            dV[pp] += w * u[pp];
+          } else {
+            du[pp] += T(0.5) * w * g[q][qq];
+            du[qq] += T(0.5) * w * g[q][pp];
+            dV[qq] += T(0.5) * w * u[pp];
+            dV[pp] += T(0.5) * w * u[qq];
+          }
+        }
+        const int k = kq * 4 + q;
+        if (live && k < Kd) {
+          T* dg = dGe + e * 9 * (int64_t)Kd + k;
+#pragma unroll
+          for (int a = 0; a < 3; a++) dg[a * Kd] = dV[a];
+#pragma unroll
+          for (int s = 0; s < 6; s++) dg[(3 + s) * Kd] = dM[s];
+        }
+      }
+      for (int off = 1; off < KQ; off <<= 1)
+#pragma unroll
+        for (int d = 0; d < 3; d++) du[d] += __shfl_xor_sync(0xffffffffu, du[d], off);
+      if (live && kq == 0) {
+#pragma unroll
+        for (int b = 0; b < BMAX; b++)
+          if (b < B) dphi[e * B + b] = dp[b];
+        T dx, dy, dz;
+        unit_bwd(u[0], u[1], u[2], r, du[0], du[1], du[2], dx, dy, dz);
+        if (acc) {
+          dvec[e * 3] += dx; dvec[e * 3 + 1] += dy; dvec[e * 3 + 2] += dz;
+        } else {
+          dvec[e * 3] = dx; dvec[e * 3 + 1] = dy; dvec[e * 3 + 2] = dz;
+        }
+      }
+    }
+  }
+}
+
+// dGt[c, a, kd] = sum_{e in row a} dGe[rev e, c, kd]   (per-edge scratch (E, 9, Kd) -> planes (9, N, Kd))
+template <typename T>
+__global__ void gather_rev_k(const T* __restrict__ src, const int32_t* __restrict__ row_ptr,
+                             const int32_t* __restrict__ rev, int Kd, int64_t N, T* __restrict__ dst, int64_t total) {
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < total; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t c = q / (N * Kd);
+    const int64_t r = q - c * N * Kd;
+    const int64_t a = r / Kd;
+    const int kd = (int)(r - a * Kd);
+    T s = 0;
+    for (int e = row_ptr[a]; e < row_ptr[a + 1]; e++) s += src[((int64_t)rev[e] * 9 + c) * Kd + kd];
+    dst[q] = s;
+  }
+}
+
+// ------------------------------------------------------------------------------------------ launchers
+inline int elem_grid(int64_t n, int threads) { return grid_for(ceil_div<int64_t>(n, threads), 16); }
+
+template <typename T>
+int edge_vec(const void* pos, const int32_t* ei, const int32_t* ej, const void* shift, void* vec, int64_t E,
+             void* stream) {
+  if (E == 0) return FACEK_OK;
+  edge_vec_k<T><<<elem_grid(E, 256), 256, 0, as_stream(stream)>>>((const T*)pos, ei, ej, (const T*)shift, (T*)vec, E);
+  return launch_status("facek_edge_vec");
+}
+template <typename T>
+int edge_vec_bwd(const void* dvec, const int32_t* row_ptr, const int32_t* rev, int64_t N, void* dpos, void* stream) {
+  if (N == 0) return FACEK_OK;
+  edge_vec_bwd_k<T><<<elem_grid(N, 128), 128, 0, as_stream(stream)>>>((const T*)dvec, row_ptr, rev, N, (T*)dpos);
+  return launch_status("facek_edge_vec_bwd");
+}
+template <typename T>
+int edge_sym(const void* vec, void* Y, int64_t E, void* stream) {
+  if (E == 0) return FACEK_OK;
+  edge_sym_k<T><<<elem_grid(E, 256), 256, 0, as_stream(stream)>>>((const T*)vec, (T*)Y, E);
+  return launch_status("facek_edge_sym");
+}
+template <typename T>
+int edge_sym_bwd(const void* vec, const void* dY, void* dvec, int acc, int64_t E, void* stream) {
+  if (E == 0) return FACEK_OK;
+  edge_sym_bwd_k<T><<<elem_grid(E, 256), 256, 0, as_stream(stream)>>>((const T*)vec, (const T*)dY, (T*)dvec, acc, E);
+  return launch_status("facek_edge_sym_bwd");
+}
+
+template <typename T, int NBMAX, int HMAX, int BMAX>
+int radial_launch(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
+                  int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2,
+                  const void* b2, const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream) {
+  const size_t smem = sizeof(T) * ((size_t)H * nb + 2 * H + (size_t)n_el * n_el * H + (size_t)H * H + (size_t)B * H + B);
+  FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_radial_fwd: weights (%zu B) exceed shared memory", smem);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(radial_mlp_k<T, NBMAX, HMAX, BMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  radial_mlp_k<T, NBMAX, HMAX, BMAX><<<grid_for(ceil_div<int64_t>(E, 128), 4), 128, smem, as_stream(stream)>>>(
+      (const T*)vec, ei, ej, zidx, n_el, (T)rc, nb, H, B, (const T*)w1, (const T*)b1, (const T*)pair, (const T*)w2,
+      (const T*)b2, (const T*)w3, (const T*)b3, (T*)phi, (T*)dphidr, E);
+  return launch_status("facek_radial_fwd");
+}
+
+template <typename T>
+int radial_fwd(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
+               int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2, const void* b2,
+               const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream) {
+  if (E == 0) return FACEK_OK;
+  FACEK_CHECK_ARG(H <= 64 && B <= 32 && nb <= 16, "facek_radial_fwd: H=%d B=%d nb=%d exceed 64/32/16", H, B, nb);
+  if (nb <= 8 && B <= 16)
+    return radial_launch<T, 8, 64, 16>(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
+                                       dphidr, E, stream);
+  if (B <= 16)
+    return radial_launch<T, 16, 64, 16>(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
+                                        dphidr, E, stream);
+  return radial_launch<T, 16, 64, 32>(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
+                                      dphidr, E, stream);
+}
+
+template <typename T>
+int radial_spline(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
+                  int G, double dr, int B, const void* Tab, const void* dTab, void* phi, void* dphidr, int64_t E,
+                  void* stream) {
+  if (E == 0) return FACEK_OK;
+  radial_spline_k<T, 32><<<elem_grid(E, 256), 256, 0, as_stream(stream)>>>(
+      (const T*)vec, ei, ej, zidx, n_el, (T)rc, G, (T)dr, B, (const T*)Tab, (const T*)dTab, (T*)phi, (T*)dphidr, E);
+  return launch_status("facek_radial_spline_fwd");
+}
+
+template <typename T>
+int radial_bwd(const void* vec, const void* dphi, const void* dphidr, int B, void* dvec, int acc, int64_t E,
+               void* stream) {
+  if (E == 0) return FACEK_OK;
+  radial_bwd_k<T><<<elem_grid(E, 256), 256, 0, as_stream(stream)>>>((const T*)vec, (const T*)dphi,
+                                                                     (const T*)dphidr, B, (T*)dvec, acc, E);
+  return launch_status("facek_radial_bwd");
+}
+
+template <typename T>
+int msg_fwd(const void* Y, const int32_t* ei, const int32_t* ej, const void* TJ, const void* TI, int nc, int K,
+            void* msg, int64_t N, int64_t E, void* stream) {
+  if (E == 0) return FACEK_OK;
+  const int64_t EK = E * K;
+  edge_msg_k<T><<<elem_grid(EK, 256), 256, 0, as_stream(stream)>>>((const T*)Y, ei, ej, (const T*)TJ, (const T*)TI,
+                                                                    nc, K, N, (T*)msg, EK);
+  return launch_status("facek_edge_msg_fwd");
+}
+
+template <typename T>
+int msg_bwd(const void* Y, const int32_t* ei, const int32_t* ej, const void* TJ, const void* TI, const void* dmsg,
+            const int32_t* row_ptr, const int32_t* rev, int nc, int K, void* dY, int acc, void* dTJ, void* dTI,
+            int64_t N, int64_t E, void* stream) {
+  if (E > 0 && dY) {
+    edge_msg_bwd_dy_k<T><<<grid_for(ceil_div<int64_t>(E, 8), 16), 256, 0, as_stream(stream)>>>(
+        ei, ej, (const T*)TJ, (const T*)TI, (const T*)dmsg, nc, K, N, (T*)dY, acc, E);
+    int st = launch_status("facek_edge_msg_bwd(dY)");
+    if (st) return st;
+  }
+  if (N > 0) {
+    const int64_t NK = N * K;
+    edge_msg_bwd_tables_k<T><<<elem_grid(NK, 128), 128, 0, as_stream(stream)>>>((const T*)Y, (const T*)dmsg, row_ptr,
+                                                                                 rev, nc, K, (T*)dTJ, (T*)dTI, NK);
+    return launch_status("facek_edge_msg_bwd(tables)");
+  }
+  return FACEK_OK;
+}
+
+template <typename T>
+int transport_fwd(const void* phi, const void* vec, const int32_t* ej, const void* Gt, const int32_t* row_ptr,
+                  void* DT, int64_t N, int B, int Kd, void* stream) {
+  if (N == 0) return FACEK_OK;
+  const int threads = ceil_div((B / 4) * Kd, 32) * 32;
+  FACEK_CHECK_ARG(threads <= 256, "facek_transport_fwd: B*Kd/4 = %d threads > 256", (B / 4) * Kd);
+  const size_t smem = sizeof(T) * TR_TILE * ((size_t)B + (size_t)Kd * 18);
+  if (smem > 48 * 1024) cudaFuncSetAttribute(transport_fwd_k<T>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  transport_fwd_k<T><<<grid_for(N, 8), threads, smem, as_stream(stream)>>>((const T*)phi, (const T*)vec, ej,
+                                                                           (const T*)Gt, row_ptr, (T*)DT, N, B, Kd);
+  return launch_status("facek_transport_fwd");
+}
+
+template <typename T>
+int transport_bwd(const void* phi, const void* vec, const int32_t* ej, const void* Gt, const void* dT1,
+                  const void* dT2, const int32_t* row_ptr, const int32_t* rev, void* dphi, void* dvec, int acc,
+                  void* dGe, void* dGt, int64_t N, int64_t E, int B, int Kd, void* stream) {
+  if (N == 0) return FACEK_OK;
+  int KQ = 1;
+  while (KQ * 4 < Kd) KQ <<= 1;
+  FACEK_CHECK_ARG(KQ <= 32, "facek_transport_bwd: Kd=%d too large", Kd);
+  const size_t smem = sizeof(T) * 18 * (size_t)B * Kd;
+  FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_transport_bwd: gradient tile %zu B exceeds shared memory",
+                  smem);
+  if (E > 0) {
+    if (B <= 16) {
+      if (smem > 48 * 1024)
+        cudaFuncSetAttribute(transport_bwd_k<T, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      transport_bwd_k<T, 16><<<grid_for(N, 4), 128, smem, as_stream(stream)>>>(
+          (const T*)phi, (const T*)vec, ej, (const T*)Gt, (const T*)dT1, (const T*)dT2, row_ptr, (T*)dphi, (T*)dvec,
+          acc, (T*)dGe, N, B, Kd, KQ);
+    } else {
+      FACEK_CHECK_ARG(B <= 32, "facek_transport_bwd: B=%d > 32", B);
+      if (smem > 48 * 1024)
+        cudaFuncSetAttribute(transport_bwd_k<T, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      transport_bwd_k<T, 32><<<grid_for(N, 4), 128, smem, as_stream(stream)>>>(
+          (const T*)phi, (const T*)vec, ej, (const T*)Gt, (const T*)dT1, (const T*)dT2, row_ptr, (T*)dphi, (T*)dvec,
+          acc, (T*)dGe, N, B, Kd, KQ);
+    }
+    int st = launch_status("facek_transport_bwd");
+    if (st) return st;
+  }
+  const int64_t total = 9 * N * Kd;
+  gather_rev_k<T><<<elem_grid(total, 256), 256, 0, as_stream(stream)>>>((const T*)dGe, row_ptr, rev, Kd, N, (T*)dGt,
+                                                                        total);
+  return launch_status("facek_transport_bwd(gather)");
+}
+
+}  // namespace
+}  // namespace facek
+
+using namespace facek;
+
+extern "C" int facek_edge_vec(int dtype, const void* pos, const int32_t* ei, const int32_t* ej, const void* shift,
+                              void* vec, int64_t E, void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && (E == 0 || (pos && ei && ej && shift && vec)), "facek_edge_vec: bad arguments");
+  return FACEK_DISPATCH(dtype, edge_vec, pos, ei, ej, shift, vec, E, stream);
+}
+extern "C" int facek_edge_vec_bwd(int dtype, const void* dvec, const int32_t* row_ptr, const int32_t* rev, int64_t N,
+                                  void* dpos, void* stream) {
+  FACEK_CHECK_ARG(N >= 0 && (N == 0 || (dvec && row_ptr && rev && dpos)), "facek_edge_vec_bwd: bad arguments");
+  return FACEK_DISPATCH(dtype, edge_vec_bwd, dvec, row_ptr, rev, N, dpos, stream);
+}
+extern "C" int facek_edge_sym(int dtype, const void* vec, void* Y, int64_t E, void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && (E == 0 || (vec && Y)), "facek_edge_sym: bad arguments");
+  return FACEK_DISPATCH(dtype, edge_sym, vec, Y, E, stream);
+}
+extern "C" int facek_edge_sym_bwd(int dtype, const void* vec, const void* dY, void* dvec, int32_t accumulate, int64_t E,
+                                  void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && (E == 0 || (vec && dY && dvec)), "facek_edge_sym_bwd: bad arguments");
+  return FACEK_DISPATCH(dtype, edge_sym_bwd, vec, dY, dvec, accumulate, E, stream);
+}
+extern "C" int facek_radial_fwd(int dtype, const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx,
+                                int32_t n_el, double rc, int32_t nb, int32_t H, int32_t B, const void* w1,
+                                const void* b1, const void* pair, const void* w2, const void* b2, const void* w3,
+                                const void* b3, void* phi, void* dphidr, int64_t E, void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && n_el > 0 && rc > 0 && nb > 0 && H > 0 && B > 0, "facek_radial_fwd: bad sizes");
+  FACEK_CHECK_ARG(E == 0 || (vec && ei && ej && zidx && w1 && b1 && pair && w2 && b2 && w3 && b3 && phi && dphidr),
+                  "facek_radial_fwd: null tensor");
+  return FACEK_DISPATCH(dtype, radial_fwd, vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
+                        dphidr, E, stream);
+}
+extern "C" int facek_radial_spline_fwd(int dtype, const void* vec, const int32_t* ei, const int32_t* ej,
+                                       const int32_t* zidx, int32_t n_el, double rc, int32_t G, double dr, int32_t B,
+                                       const void* T, const void* dT, void* phi, void* dphidr, int64_t E,
+                                       void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && n_el > 0 && G >= 2 && dr > 0 && B > 0, "facek_radial_spline_fwd: bad sizes");
+  FACEK_CHECK_ARG(E == 0 || (vec && ei && ej && zidx && T && dT && phi && dphidr), "facek_radial_spline_fwd: null");
+  return FACEK_DISPATCH(dtype, radial_spline, vec, ei, ej, zidx, n_el, rc, G, dr, B, T, dT, phi, dphidr, E, stream);
+}
+extern "C" int facek_radial_bwd(int dtype, const void* vec, const void* dphi, const void* dphidr, int32_t B, void* dvec,
+                                int32_t accumulate, int64_t E, void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && B > 0 && (E == 0 || (vec && dphi && dphidr && dvec)), "facek_radial_bwd: bad arguments");
+  return FACEK_DISPATCH(dtype, radial_bwd, vec, dphi, dphidr, B, dvec, accumulate, E, stream);
+}
+extern "C" int facek_edge_msg_fwd(int dtype, const void* Y, const int32_t* ei, const int32_t* ej, const void* TJ,
+                                  const void* TI, int32_t nc, int32_t K, void* msg, int64_t N, int64_t E,
+                                  void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && N >= 0 && nc >= 1 && nc <= 10 && K > 0, "facek_edge_msg_fwd: bad sizes nc=%d K=%d", nc,
+                  K);
+  FACEK_CHECK_ARG(E == 0 || (Y && ei && ej && TJ && msg), "facek_edge_msg_fwd: null tensor");
+  return FACEK_DISPATCH(dtype, msg_fwd, Y, ei, ej, TJ, TI, nc, K, msg, N, E, stream);
+}
+extern "C" int facek_edge_msg_bwd(int dtype, const void* Y, const int32_t* ei, const int32_t* ej, const void* TJ,
+                                  const void* TI, const void* dmsg, const int32_t* row_ptr, const int32_t* rev,
+                                  int32_t nc, int32_t K, void* dY, int32_t accumulate, void* dTJ, void* dTI, int64_t N,
+                                  int64_t E, void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && N >= 0 && nc >= 1 && nc <= 10 && K > 0, "facek_edge_msg_bwd: bad sizes");
+  FACEK_CHECK_ARG(row_ptr && rev && dTJ && (E == 0 || (Y && ei && ej && TJ && dmsg)), "facek_edge_msg_bwd: null");
+  return FACEK_DISPATCH(dtype, msg_bwd, Y, ei, ej, TJ, TI, dmsg, row_ptr, rev, nc, K, dY, accumulate, dTJ, dTI, N, E,
+                        stream);
+}
+extern "C" int facek_transport_fwd(int dtype, const void* phi, const void* vec, const int32_t* ej, const void* Gt,
+                                   const int32_t* row_ptr, void* DT, int64_t N, int32_t B, int32_t Kd, void* stream) {
+  FACEK_CHECK_ARG(N >= 0 && B > 0 && B % 4 == 0 && Kd > 0, "facek_transport_fwd: need B %% 4 == 0 (B=%d)", B);
+  FACEK_CHECK_ARG(N == 0 || (phi && vec && ej && Gt && row_ptr && DT), "facek_transport_fwd: null tensor");
+  return FACEK_DISPATCH(dtype, transport_fwd, phi, vec, ej, Gt, row_ptr, DT, N, B, Kd, stream);
+}
+extern "C" int facek_transport_bwd(int dtype, const void* phi, const void* vec, const int32_t* ej, const void* Gt,
+                                   const void* dT1, const void* dT2, const int32_t* row_ptr, const int32_t* rev,
+                                   void* dphi, void* dvec, int32_t accumulate, void* dGt_edge, void* dGt, int64_t N,
+                                   int64_t E, int32_t B, int32_t Kd, void* stream) {
+  FACEK_CHECK_ARG(N >= 0 && E >= 0 && B > 0 && Kd > 0, "facek_transport_bwd: bad sizes");
+  FACEK_CHECK_ARG(row_ptr && rev && dGt && (E == 0 || (phi && vec && ej && Gt && dT1 && dT2 && dphi && dvec &&
+                                                       dGt_edge)),
+                  "facek_transport_bwd: null tensor");
+  return FACEK_DISPATCH(dtype, transport_bwd, phi, vec, ej, Gt, dT1, dT2, row_ptr, rev, dphi, dvec, accumulate,
+                        dGt_edge, dGt, N, E, B, Kd, stream);
+}

@@ -1,1 +1,551 @@
-"""placeholder"""
+"""FACE energy+force engine on libfacek.so.
+
+Each edge- and node-level hot op is a torch.autograd.Function over one C-ABI kernel pair (forward + analytic
+backward); torch autograd only sequences them and sums their gradient contributions, and cuBLAS runs the
+channel-mixing GEMMs.  The forward follows face-mlip's FACE.forward / FactorBlock pass by pass
+(face/model.py:665-695, :310-339, :460-534, :204-308); the layouts differ where that removes copies:
+
+Every multi-component per-atom tensor is stored component-major, (components, N, channels), so each rank block
+is one contiguous (k_l*N, channels) GEMM operand and no autograd slice ever zero-fills a full-size gradient:
+  D            (20, N, B*K) density, rank blocks D[0:1] D[1:4] D[4:10] D[10:20]
+  A_l          (k_l, N, C)  (the reference keeps (N, C, k_l) and transposes around every Linear)
+  y_l          (k_l, N, 3C) projections, read in place by the node kernel; V (3,N,C), Ms (6,N,C)
+  messages     msg[e] = sum_{c<nc} Y[e,c] (TJ[c,j] + TI[c,i]) with per-atom tables TJ/TI (nc, N, K) that fold msg(h),
+               the dir_mix weights and the Y2 weights [1,1,1,2,2,2] (face/model.py:473-494 re-associated)
+  transport    two planes (3, N, 2*B*Kd) and (6, N, 2*B*Kd), columns (t, b, kd); tmix1/tmix2 columns permuted
+               once to that order (face/model.py:525-533)
+"""
+import math
+
+import numpy as np
+import torch
+import torch.nn.functional as F
+
+from . import _lib
+from .neighbors import graph_from_padded
+
+KE = 14.399645                                      # face/electrostatics.py:20
+Y2W = (1.0, 1.0, 1.0, 2.0, 2.0, 2.0)                # face/cartesian.py:81
+RANK = [(0, 1), (1, 4), (4, 10), (10, 20)]
+
+
+def _p(t):
+    return _lib.ptr(t)
+
+
+def _tag(t):
+    return _lib.dtype_tag(t)
+
+
+# ============================================================================================ edge Functions
+class EdgeVec(torch.autograd.Function):
+    """vec[e] = pos[ej] - pos[ei] + shift[e]; adjoint = the atomic-free force gather."""
+
+    @staticmethod
+    def forward(ctx, pos, gr):
+        pos = pos.detach().contiguous()
+        E = gr["ei"].numel()
+        vec = torch.empty(E, 3, dtype=pos.dtype, device=pos.device)
+        _lib.call("facek_edge_vec", _tag(pos), _p(pos), _p(gr["ei"]), _p(gr["ej"]), _p(gr["shift"]), _p(vec), E,
+                  _lib.stream())
+        ctx.gr = gr
+        ctx.N = pos.shape[0]
+        return vec
+
+    @staticmethod
+    def backward(ctx, dvec):
+        dvec = dvec.contiguous()
+        dpos = torch.empty(ctx.N, 3, dtype=dvec.dtype, device=dvec.device)
+        _lib.call("facek_edge_vec_bwd", _tag(dvec), _p(dvec), _p(ctx.gr["row_ptr"]), _p(ctx.gr["rev"]), ctx.N,
+                  _p(dpos), _lib.stream())
+        return dpos, None
+
+
+class EdgeSym(torch.autograd.Function):
+    """Y[e] = the 20 symmetric monomials of u = vec/|vec| (face/cartesian.py:34-46)."""
+
+    @staticmethod
+    def forward(ctx, vec):
+        E = vec.shape[0]
+        Y = torch.empty(E, 20, dtype=vec.dtype, device=vec.device)
+        _lib.call("facek_edge_sym", _tag(vec), _p(vec), _p(Y), E, _lib.stream())
+        ctx.save_for_backward(vec)
+        return Y
+
+    @staticmethod
+    def backward(ctx, dY):
+        (vec,) = ctx.saved_tensors
+        dY = dY.contiguous()
+        dvec = torch.empty_like(vec)
+        _lib.call("facek_edge_sym_bwd", _tag(vec), _p(vec), _p(dY), _p(dvec), 0, vec.shape[0], _lib.stream())
+        return dvec
+
+
+class Radial(torch.autograd.Function):
+    """phi = radial MLP (or spline) x envelope per edge; dphi/dr from forward-mode differentiation."""
+
+    @staticmethod
+    def forward(ctx, vec, gr, blk):
+        E = vec.shape[0]
+        B = blk["B"]
+        phi = torch.empty(E, B, dtype=vec.dtype, device=vec.device)
+        dphidr = torch.empty_like(phi)
+        if blk.get("spline") is not None:
+            Tt, dTt, dr = blk["spline"]
+            _lib.call("facek_radial_spline_fwd", _tag(vec), _p(vec), _p(gr["ei"]), _p(gr["ej"]), _p(gr["zidx"]),
+                      blk["n_el"], blk["rc"], Tt.shape[1], dr, B, _p(Tt), _p(dTt), _p(phi), _p(dphidr), E,
+                      _lib.stream())
+        else:
+            _lib.call("facek_radial_fwd", _tag(vec), _p(vec), _p(gr["ei"]), _p(gr["ej"]), _p(gr["zidx"]),
+                      blk["n_el"], blk["rc"], blk["nb"], blk["H"], B, _p(blk["w1"]), _p(blk["b1"]), _p(blk["pair"]),
+                      _p(blk["w2"]), _p(blk["b2"]), _p(blk["w3"]), _p(blk["b3"]), _p(phi), _p(dphidr), E,
+                      _lib.stream())
+        ctx.save_for_backward(vec, dphidr)
+        return phi
+
+    @staticmethod
+    def backward(ctx, dphi):
+        vec, dphidr = ctx.saved_tensors
+        dphi = dphi.contiguous()
+        dvec = torch.empty_like(vec)
+        _lib.call("facek_radial_bwd", _tag(vec), _p(vec), _p(dphi), _p(dphidr), dphi.shape[1], _p(dvec), 0,
+                  vec.shape[0], _lib.stream())
+        return dvec, None, None
+
+
+class EdgeMsg(torch.autograd.Function):
+    """msg[e,k] = sum_{c<nc} Y[e,c] (TJ[ej,c,k] + TI[ei,c,k])."""
+
+    @staticmethod
+    def forward(ctx, Y, TJ, TI, gr):
+        E = Y.shape[0]
+        nc, N, K = TJ.shape
+        TJ = TJ.contiguous()
+        TI = TI.contiguous() if TI is not None else None
+        msg = torch.empty(E, K, dtype=Y.dtype, device=Y.device)
+        _lib.call("facek_edge_msg_fwd", _tag(Y), _p(Y), _p(gr["ei"]), _p(gr["ej"]), _p(TJ), _p(TI), nc, K, _p(msg),
+                  N, E, _lib.stream())
+        ctx.save_for_backward(Y, TJ, TI)
+        ctx.gr = gr
+        return msg
+
+    @staticmethod
+    def backward(ctx, dmsg):
+        Y, TJ, TI = ctx.saved_tensors
+        gr = ctx.gr
+        nc, N, K = TJ.shape
+        E = Y.shape[0]
+        dmsg = dmsg.contiguous()
+        dY = torch.empty_like(Y)
+        dTJ = torch.empty_like(TJ)
+        dTI = torch.empty_like(TI) if TI is not None else None
+        _lib.call("facek_edge_msg_bwd", _tag(Y), _p(Y), _p(gr["ei"]), _p(gr["ej"]), _p(TJ), _p(TI), _p(dmsg),
+                  _p(gr["row_ptr"]), _p(gr["rev"]), nc, K, _p(dY), 0, _p(dTJ), _p(dTI), N, E, _lib.stream())
+        return dY, dTJ, dTI, None
+
+
+class Density(torch.autograd.Function):
+    """D[x, i, b*K+k] = sum_{e in row i} phi[e,b] msg[e,k] Y[e,x] (CSR rows), returned as the four rank blocks
+    (k_l, N, B*K) of one (20, N, B*K) buffer."""
+
+    @staticmethod
+    def forward(ctx, phi, msg, Y, gr):
+        N = gr["row_ptr"].numel() - 1
+        B, K = phi.shape[1], msg.shape[1]
+        D = torch.empty(20, N, B * K, dtype=phi.dtype, device=phi.device)
+        _lib.call("facek_density_xm_fwd", _tag(phi), _p(phi), _p(msg), _p(Y), _p(D), N, B, K, _p(gr["row_ptr"]),
+                  _lib.stream())
+        ctx.save_for_backward(phi, msg, Y)
+        ctx.gr = gr
+        return tuple(D[a:b] for a, b in RANK)
+
+    @staticmethod
+    def backward(ctx, *dD):
+        phi, msg, Y = ctx.saved_tensors
+        N = ctx.gr["row_ptr"].numel() - 1
+        B, K = phi.shape[1], msg.shape[1]
+        G = [g.contiguous() if g is not None else torch.zeros(b - a, N, B * K, dtype=phi.dtype, device=phi.device)
+             for g, (a, b) in zip(dD, RANK)]
+        dphi, dmsg, dY = torch.empty_like(phi), torch.empty_like(msg), torch.empty_like(Y)
+        _lib.call("facek_density_xm_bwd", _tag(phi), _p(phi), _p(msg), _p(Y), *[_p(g) for g in G], _p(dphi),
+                  _p(dmsg), _p(dY), N, B, K, _p(ctx.gr["row_ptr"]), _lib.stream())
+        return dphi, dmsg, dY, None
+
+
+class Transport(torch.autograd.Function):
+    """Transport sums as two planes (3, N, 2*B*Kd) [V, M u] and (6, N, 2*B*Kd) [M, sym(u V)], Gt (9, N, Kd)."""
+
+    @staticmethod
+    def forward(ctx, phi, vec, Gt, gr):
+        N = gr["row_ptr"].numel() - 1
+        B, Kd = phi.shape[1], Gt.shape[2]
+        Gt = Gt.contiguous()
+        DT = torch.empty(9 * N * 2 * B * Kd, dtype=phi.dtype, device=phi.device)
+        _lib.call("facek_transport_fwd", _tag(phi), _p(phi), _p(vec), _p(gr["ej"]), _p(Gt), _p(gr["row_ptr"]),
+                  _p(DT), N, B, Kd, _lib.stream())
+        ctx.save_for_backward(phi, vec, Gt)
+        ctx.gr = gr
+        h = 3 * N * 2 * B * Kd
+        return DT[:h].view(3, N, 2 * B * Kd), DT[h:].view(6, N, 2 * B * Kd)
+
+    @staticmethod
+    def backward(ctx, dT1, dT2):
+        phi, vec, Gt = ctx.saved_tensors
+        gr = ctx.gr
+        N = gr["row_ptr"].numel() - 1
+        E = phi.shape[0]
+        B, Kd = phi.shape[1], Gt.shape[2]
+        z = lambda k: torch.zeros(k, N, 2 * B * Kd, dtype=phi.dtype, device=phi.device)
+        dT1 = dT1.contiguous() if dT1 is not None else z(3)
+        dT2 = dT2.contiguous() if dT2 is not None else z(6)
+        dphi = torch.empty_like(phi)
+        dvec = torch.empty_like(vec)
+        dGe = torch.empty(E, 9, Kd, dtype=phi.dtype, device=phi.device)
+        dGt = torch.empty_like(Gt)
+        _lib.call("facek_transport_bwd", _tag(phi), _p(phi), _p(vec), _p(gr["ej"]), _p(Gt), _p(dT1), _p(dT2),
+                  _p(gr["row_ptr"]), _p(gr["rev"]), _p(dphi), _p(dvec), 0, _p(dGe), _p(dGt), N, E, B, Kd,
+                  _lib.stream())
+        return dphi, dvec, dGt, None
+
+
+class NodeAlgebraEngine(torch.autograd.Function):
+    """Invariant families + gated products from the (N, k_l, 3C) projections."""
+
+    @staticmethod
+    def forward(ctx, y0, y1, y2, y3, a, b, eq, max_body):
+        _, N, C3 = y1.shape
+        C = C3 // 3
+        ys = [y.contiguous() for y in (y0, y1, y2, y3)]
+        inv9 = torch.empty(N, 9 * C, dtype=y1.dtype, device=y1.device)
+        V = torch.empty(3, N, C, dtype=y1.dtype, device=y1.device) if eq else y1.new_zeros(0)
+        Ms = torch.empty(6, N, C, dtype=y1.dtype, device=y1.device) if eq else y1.new_zeros(0)
+        _lib.call("facek_node_engine_fwd", _tag(y1), *[_p(y) for y in ys], _p(a), _p(b), _p(inv9),
+                  _p(V) if eq else None, _p(Ms) if eq else None, N, C, int(eq), int(max_body), _lib.stream())
+        ctx.save_for_backward(*ys)
+        ctx.a, ctx.b, ctx.eq, ctx.max_body = a, b, eq, max_body
+        if not eq:
+            ctx.mark_non_differentiable(V, Ms)
+        return inv9, V, Ms
+
+    @staticmethod
+    def backward(ctx, g9, gV, gMs):
+        ys = ctx.saved_tensors
+        _, N, C3 = ys[1].shape
+        C = C3 // 3
+        g9 = g9.contiguous() if g9 is not None else torch.zeros(N, 9 * C, dtype=ys[1].dtype, device=ys[1].device)
+        if ctx.eq:
+            gV = gV.contiguous() if gV is not None else torch.zeros(3, N, C, dtype=g9.dtype, device=g9.device)
+            gMs = gMs.contiguous() if gMs is not None else torch.zeros(6, N, C, dtype=g9.dtype, device=g9.device)
+        dys = [torch.empty_like(y) for y in ys]
+        _lib.call("facek_node_engine_bwd", _tag(g9), *[_p(y) for y in ys], _p(ctx.a), _p(ctx.b), _p(g9),
+                  _p(gV) if ctx.eq else None, _p(gMs) if ctx.eq else None, *[_p(d) for d in dys], N, C, int(ctx.eq),
+                  int(ctx.max_body), _lib.stream())
+        return (*dys, None, None, None, None)
+
+
+class CoulombReal(torch.autograd.Function):
+    """e_row[i] = 1/2 q_i sum_{e in row i} q_j (erf(r/gamma) - erf(r/gp))/r (face/electrostatics.py:91-92,125-127)."""
+
+    @staticmethod
+    def forward(ctx, vec, q, gr, gamma, gp):
+        N = q.shape[0]
+        q = q.contiguous()
+        e_row = torch.empty_like(q)
+        _lib.call("facek_coulomb_real_fwd", _tag(q), _p(vec), _p(gr["row_ptr"]), _p(gr["ej"]), _p(q), gamma, gp, N,
+                  _p(e_row), _lib.stream())
+        ctx.save_for_backward(vec, q)
+        ctx.gr, ctx.gamma, ctx.gp = gr, gamma, gp
+        return e_row
+
+    @staticmethod
+    def backward(ctx, g_row):
+        vec, q = ctx.saved_tensors
+        g_row = g_row.contiguous()
+        dvec = torch.empty_like(vec)
+        dq = torch.empty_like(q)
+        _lib.call("facek_coulomb_real_bwd", _tag(q), _p(vec), _p(ctx.gr["row_ptr"]), _p(ctx.gr["ej"]), _p(q),
+                  ctx.gamma, ctx.gp, _p(g_row), q.shape[0], _p(dvec), 0, _p(dq), _lib.stream())
+        return dvec, dq, None, None, None
+
+
+_BMOD = {}
+
+
+def bspline_modulus2(n, dtype, device):
+    """|b(m)|^-2 of the order-4 Euler spline (Essmann et al. 1995; face/electrostatics.py:44-51)."""
+    key = (n, dtype, str(device))
+    if key not in _BMOD:
+        m = np.arange(n, dtype=np.float64)
+        ang = 2 * np.pi * m[:, None] * np.arange(3)[None] / n
+        w = np.array([1 / 6, 4 / 6, 1 / 6])
+        den = (w * np.cos(ang)).sum(-1) ** 2 + (w * np.sin(ang)).sum(-1) ** 2
+        _BMOD[key] = torch.as_tensor(1.0 / np.maximum(den, 1e-10), dtype=dtype, device=device)
+    return _BMOD[key]
+
+
+class PMERecip(torch.autograd.Function):
+    """Smooth-PME reciprocal energy of one periodic structure (face/electrostatics.py:54-77): spread -> cuFFT
+    (torch.fft.rfftn) -> Green's function x |b|^2 (energy + convolved spectrum) -> irfftn -> gather."""
+
+    @staticmethod
+    def forward(ctx, pos, q, cell64, gp, mesh):
+        pos, q = pos.detach().contiguous(), q.detach().contiguous()
+        n0, n1, n2 = mesh
+        inv = np.linalg.inv(cell64)
+        vol = abs(float(np.linalg.det(cell64)))
+        invd = _lib.doubles(inv.reshape(-1))
+        grid = torch.zeros(n0 * n1 * n2, dtype=pos.dtype, device=pos.device)
+        _lib.call("facek_pme_spread", _tag(pos), _p(pos), _p(q), pos.shape[0], invd, n0, n1, n2, _p(grid),
+                  _lib.stream())
+        spec = torch.view_as_real(torch.fft.rfftn(grid.view(n0, n1, n2))).contiguous()
+        bmod = torch.cat([bspline_modulus2(n, pos.dtype, pos.device) for n in (n0, n1, n2)])
+        energy = torch.zeros(1, dtype=torch.float64, device=pos.device)
+        conv = torch.empty_like(spec)
+        _lib.call("facek_pme_green", _tag(pos), _p(spec), n0, n1, n2, invd, float(gp), vol, _p(bmod), _p(energy),
+                  _p(conv), _lib.stream())
+        pot = torch.fft.irfftn(torch.view_as_complex(conv), s=(n0, n1, n2)).contiguous()
+        ctx.save_for_backward(pos, q, pot)
+        ctx.inv, ctx.mesh = inv, mesh
+        return energy.to(pos.dtype)[0]
+
+    @staticmethod
+    def backward(ctx, g):
+        pos, q, pot = ctx.saved_tensors
+        n0, n1, n2 = ctx.mesh
+        potg = (pot * g).contiguous()
+        dq = torch.empty_like(q)
+        dpos = torch.empty_like(pos)
+        _lib.call("facek_pme_gather", _tag(pos), _p(pos), _p(q), pos.shape[0], _lib.doubles(ctx.inv.reshape(-1)), n0,
+                  n1, n2, _p(potg), 1.0, _p(dq), _p(dpos), _lib.stream())
+        return dpos, dq, None, None, None
+
+
+# ============================================================================================ weights
+def _lin(model, mod, dtype, dev):
+    w = mod.weight.detach()
+    if model.unit:
+        w = w * w.shape[1] ** -0.5
+    b = mod.bias.detach().to(dtype=dtype, device=dev).contiguous() if getattr(mod, "bias", None) is not None else None
+    return w.to(dtype=dtype, device=dev).contiguous(), b
+
+
+def prepare(model, dtype, dev):
+    """Effective (unit-scaled), detached, layout-ready weights; cached until the model changes."""
+    key = (dtype, str(dev), model.max_body, tuple(id(s) for s in model.spline))
+    if model._prepared is not None and model._prepared["key"] == key:
+        return model._prepared
+    for k, v in model.switches.items():
+        if v:
+            raise NotImplementedError(k)
+    P = {"key": key}
+    d = lambda t: t.detach().to(dtype=dtype, device=dev).contiguous()
+    P["zmap"] = model.zmap.to(dev)
+    P["embed"] = d(model.embed.weight)
+    P["E0"], P["scale"], P["avg_nb"] = d(model.E0), d(model.scale), d(model.avg_nb)
+    n_el = len(model.elements)
+    blocks = []
+    for t, blk in enumerate(model.blocks):
+        C, B, K, Kd = blk.C, blk.B, blk.Km, blk.Kd
+        q = {"B": B, "K": K, "Kd": Kd, "C": C, "n_el": n_el, "rc": float(model.rc), "nb": model.n_basis,
+             "directional": blk.directional, "transport": blk.transport, "eq_in": blk.eq_in, "eq_out": blk.eq_out}
+        q["w1"], q["b1"] = _lin(model, blk.rad_in, dtype, dev)
+        q["H"] = q["w1"].shape[0]
+        q["pair"] = d(blk.pair.weight)
+        q["w2"], q["b2"] = _lin(model, blk.radial[0], dtype, dev)
+        q["w3"], q["b3"] = _lin(model, blk.radial[2], dtype, dev)
+        sp = model.spline[t]
+        q["spline"] = None if sp is None else (d(sp[0]), d(sp[1]), float(sp[2]))
+        q["msg_w"], q["msg_b"] = _lin(model, blk.msg, dtype, dev)
+        q["mixT"] = [(_lin(model, blk.mix[l], dtype, dev)[0]).t().contiguous() for l in range(4)]      # (BK, C)
+        q["projT"] = [(_lin(model, blk.proj[l], dtype, dev)[0]).t().contiguous() for l in range(4)]    # (cin, 3C)
+        q["elem_scale"] = d(blk.elem_scale.weight)
+        q["norm"] = blk.norm_kind
+        if blk.norm_kind == "layer":
+            q["ln_w"], q["ln_b"], q["ln_eps"] = d(blk.norm.weight), d(blk.norm.bias), blk.norm.eps
+        elif blk.norm_kind == "affine":
+            q["ln_w"], q["ln_b"] = d(blk.norm.w), d(blk.norm.b)
+        q["out"] = [_lin(model, blk.out[i], dtype, dev) for i in (0, 2, 4)]
+        if blk.eq_out:
+            q["vpath"], q["mpath"] = d(blk.vpath), d(blk.mpath)
+            q["gate"] = _lin(model, blk.gate, dtype, dev)
+        if blk.directional:
+            wd, bd = _lin(model, blk.dir_mix, dtype, dev)                                 # (K, 4Kd)
+            q["dir"] = [wd[:, i * Kd:(i + 1) * Kd].t().contiguous() for i in range(4)]       # each (Kd, K)
+            q["dir_b"] = bd
+            q["pvtT"] = _lin(model, blk.pvt, dtype, dev)[0].t().contiguous()                # (cprev, nt*Kd)
+            q["pmtT"] = _lin(model, blk.pmt, dtype, dev)[0].t().contiguous()
+            q["y2w"] = torch.tensor(Y2W, dtype=dtype, device=dev)[:, None, None]
+        if blk.transport:
+            for name in ("tmix1", "tmix2"):
+                w = _lin(model, getattr(blk, name), dtype, dev)[0]                           # (C, B*2*Kd) cols (b,t,kd)
+                q[name + "T"] = w.view(C, B, 2, Kd).permute(0, 2, 1, 3).reshape(C, 2 * B * Kd).t().contiguous()
+        blocks.append(q)
+    P["blocks"] = blocks
+    if "coulomb" in model.terms:
+        tm = model.terms["coulomb"]
+        P["coulomb"] = {"h0": _lin(model, tm.head[0], dtype, dev), "h2": _lin(model, tm.head[2], dtype, dev),
+                        "gamma": float(tm.gamma), "gp": float(tm.gp), "mesh": tm.mesh}
+    model._prepared = P
+    return P
+
+
+def build_spline(model, t, n_grid=4096):
+    """Cubic Hermite tables of block t's radial MLP per element pair (face/model.py:393-405), evaluated once with
+    torch on the model's device: T (P, G, B) values, dT (P, G, B) exact r-derivatives, grid step rc/(G-1)."""
+    blk = model.blocks[t]
+    dev, dt = blk.rad_in.weight.device, blk.rad_in.weight.dtype
+    rc = float(model.rc)
+    r = torch.linspace(0, rc, n_grid, device=dev, dtype=dt).clamp_min(1e-4)
+    pairs = blk.pair.weight.detach()
+    lin = lambda mod, x: F.linear(x, mod.weight.detach() * (mod.weight.shape[1] ** -0.5 if model.unit else 1.0),
+                                  mod.bias.detach() if mod.bias is not None else None)
+    with torch.enable_grad():
+        rr = r[None].expand(pairs.shape[0], -1).clone().requires_grad_(True)
+        freq = torch.arange(1, model.n_basis + 1, device=dev, dtype=dt) * math.pi / rc
+        x = rr / rc
+        env = (1 - 28 * x ** 6 + 48 * x ** 7 - 21 * x ** 8) * (x < 1)
+        bes = torch.sin(freq * rr[..., None]) / rr[..., None] * math.sqrt(2 / rc)
+        h = F.silu(lin(blk.rad_in, bes * env[..., None]) + pairs[:, None, :])
+        T = lin(blk.radial[2], F.silu(lin(blk.radial[0], h)))
+        dT = torch.stack([torch.autograd.grad(T[..., b].sum(), rr, retain_graph=True)[0] for b in range(T.shape[-1])],
+                         -1)
+    return (T.detach().contiguous(), dT.detach().contiguous(), rc / (n_grid - 1))
+
+
+# ============================================================================================ forward
+def _layer(W, x):
+    w, b = W
+    return F.linear(x, w, b)
+
+
+def block_forward(P, t, gr, geo, h, A_sets, eq):
+    """One factorised pass (face/model.py:310-339 with FactorBlock.moments :460-534)."""
+    q = P["blocks"][t]
+    N = h.shape[0]
+    C, B, K, Kd = q["C"], q["B"], q["K"], q["Kd"]
+    vec, Y = geo["vec"], geo["Y"]
+    phi = Radial.apply(vec, gr, q)                                                   # (E, B), env included
+    msgtab = F.linear(h, q["msg_w"], q["msg_b"])                                     # (N, K)
+    Gt = None
+    if q["directional"]:
+        src1 = eq[0] if q["eq_in"] else torch.cat([A[1] for A in A_sets], 2)        # (3, N, cprev)
+        src2 = eq[1] if q["eq_in"] else torch.cat([A[2] for A in A_sets], 2)        # (6, N, cprev)
+        Vb = src1 @ q["pvtT"]                                                        # (3, N, nt*Kd)
+        Mb = src2 @ q["pmtT"]                                                        # (6, N, nt*Kd)
+        Vd, Md = Vb[..., :Kd], Mb[..., :Kd]
+        w1, w2, w3, w4 = q["dir"]
+        TJ = torch.cat([(msgtab + q["dir_b"])[None], Vd @ w1, (Md @ w2) * q["y2w"]], 0)        # (10, N, K)
+        TI = torch.cat([torch.zeros_like(msgtab)[None], Vd @ w3, (Md @ w4) * q["y2w"]], 0)
+        if q["transport"]:
+            Gt = torch.cat([Vb[..., Kd:], Mb[..., Kd:]], 0)                           # (9, N, Kd)
+        mj = EdgeMsg.apply(Y, TJ, TI, gr)
+    else:
+        mj = EdgeMsg.apply(Y, msgtab[None], None, gr)
+    D = Density.apply(phi, mj, Y, gr)                                                # 4 x (k_l, N, B*K)
+    s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1)   # (4, N, C)
+    A = [D[l] @ q["mixT"][l] for l in range(4)]                                      # (k_l, N, C)
+    if Gt is not None:
+        T1, T2 = Transport.apply(phi, vec, Gt, gr)                                   # (3|6, N, 2*B*Kd)
+        A[1] = A[1] + T1 @ q["tmix1T"]
+        A[2] = A[2] + T2 @ q["tmix2T"]
+    A = [A[l] * s[l] for l in range(4)]
+    # invariants (face/model.py:204-270): projections straight into the node kernel's layout
+    sets = A_sets + [A]
+    ys = [torch.cat([a[l] for a in sets], 2) @ q["projT"][l] for l in range(4)]     # (k_l, N, 3C)
+    a_w = q["vpath"] if q["eq_out"] else None
+    b_w = q["mpath"] if q["eq_out"] else None
+    inv, V, Ms = NodeAlgebraEngine.apply(*ys, a_w, b_w, q["eq_out"], P["max_body"])
+    if q["norm"] == "layer":
+        inv = F.layer_norm(inv, (inv.shape[1],), q["ln_w"], q["ln_b"], q["ln_eps"])
+    elif q["norm"] == "affine":
+        inv = inv * q["ln_w"] + q["ln_b"]
+    z = torch.cat([inv, h, inv.new_zeros(N, 4)], 1)
+    o = _layer(q["out"][2], F.silu(_layer(q["out"][1], F.silu(_layer(q["out"][0], z)))))
+    eq_new = None
+    if q["eq_out"]:
+        gv, gm = _layer(q["gate"], inv).chunk(2, dim=-1)
+        eq_new = (V * gv[None], Ms * gm[None])
+    return o[:, 0], h + o[:, 1:], A, eq_new
+
+
+def coulomb_term(P, gr, geo, h, pos):
+    """LatentCharges.forward, mode 'local' (face/electrostatics.py:132-176)."""
+    c = P["coulomb"]
+    chi, hard = _layer(c["h2"], F.silu(_layer(c["h0"], h))).unbind(-1)
+    J = F.softplus(hard) + 0.1
+    batch, nstr = gr["batch"], gr["nstr"]
+    invJ = 1.0 / J
+    num = torch.zeros(nstr, dtype=chi.dtype, device=chi.device).index_add(0, batch, chi * invJ)
+    den = torch.zeros(nstr, dtype=chi.dtype, device=chi.device).index_add(0, batch, invJ)
+    Q = gr["charge"].to(chi.dtype)
+    mu = (Q + num) / den
+    q = -(chi - mu[batch]) * invJ
+    gamma, gp = c["gamma"], c["gp"]
+    natoms = gr["natoms"]
+    if not all(gr["pbc"]):
+        if any(gr["pbc"]):
+            raise NotImplementedError("Coulomb term on a batch mixing periodic and non-periodic structures")
+        # molecules: dense Gaussian-charge Coulomb inside each structure (face/electrostatics.py:178-198)
+        d = torch.sqrt(((pos[:, None] - pos[None]) ** 2).sum(-1) + torch.eye(len(q), dtype=pos.dtype, device=pos.device))
+        same = (batch[:, None] == batch[None, :]) & ~torch.eye(len(q), dtype=torch.bool, device=pos.device)
+        A = torch.where(same, torch.erf(d / gamma) / d, torch.zeros_like(d))
+        return chi * q + 0.5 * J * q * q + 0.5 * KE * q * (A @ q), q
+    e_row = CoulombReal.apply(geo["vec"], q, gr, gamma, gp)
+    e_real = torch.zeros(nstr, dtype=q.dtype, device=q.device).index_add(0, batch, e_row)
+    q2 = torch.zeros(nstr, dtype=q.dtype, device=q.device).index_add(0, batch, q * q)
+    qs = torch.zeros(nstr, dtype=q.dtype, device=q.device).index_add(0, batch, q)
+    e_recip = []
+    offs = [0] + np.cumsum(natoms.tolist()).tolist()
+    for s in range(nstr):
+        cell = gr["cell64"][s]
+        mesh = c["mesh"]
+        if mesh is None:                                       # face/electrostatics.py:56-58
+            spacing = gp / 4.0
+            mesh = tuple(max(8, int(math.ceil(float(L) / spacing))) for L in np.linalg.norm(cell, axis=1))
+        sl = slice(offs[s], offs[s + 1])
+        e_recip.append(PMERecip.apply(pos[sl], q[sl], cell, gp, tuple(mesh)))
+    e_recip = torch.stack(e_recip)
+    vol = torch.as_tensor([abs(np.linalg.det(gr["cell64"][s])) for s in range(nstr)], dtype=q.dtype, device=q.device)
+    e_es = KE * (e_recip + e_real - q2 / (math.sqrt(math.pi) * gp) - 0.5 * math.pi * gp ** 2 / vol * qs ** 2)
+    return chi * q + 0.5 * J * q * q + (e_es / natoms.to(q.dtype))[batch], q
+
+
+def face_forward(model, g, forces=True):
+    """Energy (per structure), per-atom energy and forces for a graph dict (face/model.py:665-695).  `g` is either
+    the engine's CSR graph (face_b200.neighbors.build_graph) or the reference's padded dict."""
+    gr = g if "row_ptr" in g else graph_from_padded(g)
+    pos = g["pos"]
+    if not pos.is_cuda:
+        raise RuntimeError("face_b200 runs on CUDA only (no CPU path)")
+    dtype, dev = model.embed.weight.dtype, pos.device
+    P = prepare(model, dtype, dev)
+    P["max_body"] = model.max_body
+    if pos.dtype != dtype:
+        raise TypeError(f"positions are {pos.dtype}, model is {dtype}")
+    if forces and not pos.requires_grad:
+        pos.requires_grad_(True)
+    with torch.set_grad_enabled(forces):
+        zidx = P["zmap"][gr["Z"]]
+        gr = dict(gr, zidx=zidx.to(torch.int32).contiguous())
+        vec = EdgeVec.apply(pos, gr)
+        Y = EdgeSym.apply(vec)
+        geo = {"vec": vec, "Y": Y, "zidx": zidx, "avg_nb": P["avg_nb"]}
+        h = P["embed"][zidx]
+        e_at = P["E0"][zidx]
+        A_sets, eq = [], None
+        for t in range(len(P["blocks"])):
+            e, h, A, eq = block_forward(P, t, gr, geo, h, A_sets, eq)
+            A_sets.append(A)
+            e_at = e_at + P["scale"] * e
+        qv = None
+        if "coulomb" in P:
+            ea, qv = coulomb_term(P, gr, geo, h, pos)
+            e_at = e_at + ea
+        E = torch.zeros(gr["nstr"], dtype=e_at.dtype, device=dev).index_add(0, gr["batch"], e_at)
+        out = {"energy": E.detach(), "atom_energy": e_at.detach()}
+        if qv is not None:
+            out["q"] = qv.detach()
+        if forces:
+            (grad,) = torch.autograd.grad(E.sum(), pos)
+            out["forces"] = -grad
+    return out

@@ -1,0 +1,188 @@
+/* facek.h -- C ABI of libfacek.so, the B200 (sm_100a) kernels behind the face_b200 engine.
+ *
+ * Conventions (all entry points):
+ *   - plain device pointers and sizes, no framework types; the caller owns every buffer (the library never
+ *     allocates device memory), exactly like face-mlip's CuPy kernels, which receive DLPack pointers from
+ *     torch-allocated tensors (face/kernels.py:131-132, :141; face/node_kernel.py:174-176);
+ *   - `dtype` is FACEK_F32 or FACEK_F64 and applies to every floating-point buffer of the call;
+ *   - `stream` is a cudaStream_t passed as void* (the reference launches on torch's current stream,
+ *     face/kernels.py:145);
+ *   - index buffers are int32 (atoms and edges < 2^31); `row_ptr` is the CSR row offset array (N+1 entries)
+ *     of a centre-sorted edge list;
+ *   - return 0 on success, a negative FACEK_E* code otherwise; facek_last_error() gives the message.
+ *     The reference has no error reporting at all (shape limits are implicit, face/kernels.py:146,159-163).
+ */
+#ifndef FACEK_H
+#define FACEK_H
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { FACEK_F32 = 0, FACEK_F64 = 1 };
+enum { FACEK_OK = 0, FACEK_EINVAL = -1, FACEK_ELAUNCH = -2, FACEK_ETIMEOUT = -3, FACEK_EUNSUPPORTED = -4 };
+
+const char* facek_last_error(void);
+int facek_version(void);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Factorised Cartesian density  D[i, x, b*K + k] = sum_m phi[m, b] * msg[m, k] * Y[m, x],  x = 0..19.
+ * Replaces face-mlip face/kernels.py:22-54 (dens_fwd) and :56-118 (dens_bwd) behind
+ * face.kernels.factor_density (face/kernels.py:170-172).
+ * Rows: padded layout (row_ptr == NULL: row i = edges i*M .. i*M+M-1, the reference's (N,M,*) tensors)
+ * or CSR (row_ptr != NULL, M ignored).  phi (E,B), msg (E,K), Y (E,20), D / G (N,20,B*K).
+ */
+int facek_density_fwd(int dtype, const void* phi, const void* msg, const void* Y, void* D, int64_t N, int32_t M,
+                      int32_t B, int32_t K, const int32_t* row_ptr, void* stream);
+int facek_density_bwd(int dtype, const void* phi, const void* msg, const void* Y, const void* G, void* dphi,
+                      void* dmsg, void* dY, int64_t N, int32_t M, int32_t B, int32_t K, const int32_t* row_ptr,
+                      void* stream);
+/* Same contraction for the engine, component-major ("x-major") layout: D is (20, N, B*K), so the rank blocks
+ * D[0:1], D[1:4], D[4:10], D[10:20] are contiguous (k_l*N, B*K) GEMM operands for the channel maps
+ * (face/model.py:506); the backward takes the four rank gradients as separate (k_l, N, B*K) buffers G0..G3. */
+int facek_density_xm_fwd(int dtype, const void* phi, const void* msg, const void* Y, void* D, int64_t N, int32_t B,
+                         int32_t K, const int32_t* row_ptr, void* stream);
+int facek_density_xm_bwd(int dtype, const void* phi, const void* msg, const void* Y, const void* G0, const void* G1,
+                         const void* G2, const void* G3, void* dphi, void* dmsg, void* dY, int64_t N, int32_t B,
+                         int32_t K, const int32_t* row_ptr, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Node invariant algebra, reference layout.  Replaces face-mlip face/node_kernel.py:18-64 (node_fwd) and
+ * :66-151 (node_bwd) behind face.node_kernel.node_algebra (:207-209).
+ * P1,Q1,S1 (N,C,3); P2,Q2,S2 (N,C,6); P3,Q3 (N,C,10) symmetric storage; a, b (4,C) path weights (the
+ * reference transposes them to (C,4) before launch, face/node_kernel.py:173).  inv (N,C,8), V (N,C,3),
+ * Mf (N,C,3,3).  Backward: gI/gV/gM upstream (gV, gM may be NULL when eq == 0); writes the 8 input
+ * gradients and per-(atom,channel) partials da_part, db_part (N,C,4) (may be NULL when eq == 0).
+ */
+int facek_node_fwd(int dtype, const void* P1, const void* Q1, const void* S1, const void* P2, const void* Q2,
+                   const void* S2, const void* P3, const void* Q3, const void* a, const void* b, void* inv, void* V,
+                   void* Mf, int64_t N, int32_t C, int32_t eq, void* stream);
+int facek_node_bwd(int dtype, const void* P1, const void* Q1, const void* S1, const void* P2, const void* Q2,
+                   const void* S2, const void* P3, const void* Q3, const void* a, const void* b, const void* gI,
+                   const void* gV, const void* gM, void* dP1, void* dQ1, void* dS1, void* dP2, void* dQ2, void* dS2,
+                   void* dP3, void* dQ3, void* da_part, void* db_part, int64_t N, int32_t C, int32_t eq,
+                   void* stream);
+
+/* Node algebra, engine layout (component-major): the projected moments y_l = proj_l(x_l) as (k_l, N, 3C) with P,
+ * Q, S in channel blocks [0,C), [C,2C), [2C,3C) (face/model.py:227 without its transposes); writes the 9 families
+ * [P0 | i1..i8] as inv9 (N, 9C) with families above max_body zeroed (face/model.py:244-247), V (3,N,C) and
+ * Ms (6,N,C) = symmetric storage of (Mf + Mf^T)/2 (face/model.py:274-276) when eq != 0.
+ * Backward writes dy_l in the same layouts (dQ0, dS0, dS3 are zero: unused by the reference). */
+int facek_node_engine_fwd(int dtype, const void* y0, const void* y1, const void* y2, const void* y3, const void* a,
+                          const void* b, void* inv9, void* V, void* Ms, int64_t N, int32_t C, int32_t eq,
+                          int32_t max_body, void* stream);
+int facek_node_engine_bwd(int dtype, const void* y0, const void* y1, const void* y2, const void* y3, const void* a,
+                          const void* b, const void* g_inv9, const void* gV, const void* gMs, void* dy0, void* dy1,
+                          void* dy2, void* dy3, int64_t N, int32_t C, int32_t eq, int32_t max_body, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Neighbour list (cell list, fp64 distance test), replacing ase.neighborlist.neighbor_list("ijS") as called at
+ * face-mlip face/neighbors.py:12 and face/datasets.py:51 (+ the stable argsort and slot fill :14, :74-79).
+ * Edge set: every (i, j, S) with |pos[j] - pos[i] + S.cell| < rc except the zero-shift self pair; rows are
+ * centre-sorted and, within a row, in (j, S0, S1, S2) order.
+ * Periodic single structure (pbc on all axes):
+ *   facek_nlist_cell_workspace(N, cell, rc, &bytes)  size of the int32 scratch the caller provides;
+ *   facek_nlist_cell_count   -> deg (N)
+ *   (caller: row_ptr = exclusive prefix sum of deg)
+ *   facek_nlist_cell_fill    -> ei (E) centre, ej (E) neighbour, S (E,3 int32) image, shift (E,3) = S.cell in
+ *                               the model dtype (face/datasets.py:52)
+ * Non-periodic batch of structures (atoms of structure s are struct_start[s] .. struct_start[s+1]-1):
+ *   facek_nlist_batch_count / facek_nlist_batch_fill (all pairs within a structure, shift = 0).
+ * Reverse index: rev[e] = index of the edge (j, i, -S) (the list is symmetric); used by the atomic-free
+ * gathers below.
+ */
+int facek_nlist_cell_workspace(int64_t N, const double* cell, double rc, int64_t* bytes);
+int facek_nlist_cell_count(const double* pos, int64_t N, const double* cell, double rc, void* workspace,
+                           int32_t* deg, void* stream);
+int facek_nlist_cell_fill(int dtype, const double* pos, int64_t N, const double* cell, double rc, void* workspace,
+                          const int32_t* row_ptr, int32_t* ei, int32_t* ej, int32_t* S, void* shift, void* stream);
+int facek_nlist_batch_count(const double* pos, int64_t N, const int32_t* struct_start, const int32_t* atom_struct,
+                            double rc, int32_t* deg, void* stream);
+int facek_nlist_batch_fill(int dtype, const double* pos, int64_t N, const int32_t* struct_start,
+                           const int32_t* atom_struct, double rc, const int32_t* row_ptr, int32_t* ei, int32_t* ej,
+                           int32_t* S, void* shift, void* stream);
+int facek_nlist_reverse(const int32_t* row_ptr, const int32_t* ei, const int32_t* ej, const int32_t* S, int64_t N,
+                        int64_t E, int32_t* rev, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Edge geometry: vec[e] = pos[ej] - pos[ei] + shift[e] (face/model.py:670) and its adjoint, the force gather
+ * dpos[k] = sum_{e in row k} (dvec[rev[e]] - dvec[e]) (autograd through :670 and :693, without atomics).
+ * Y[e] = 20 symmetric monomials of u = vec/|vec| (face/cartesian.py:34-46, face/model.py:671-677);
+ * sym_bwd accumulates dvec += d(Y)/d(vec)^T dY.
+ */
+int facek_edge_vec(int dtype, const void* pos, const int32_t* ei, const int32_t* ej, const void* shift, void* vec,
+                   int64_t E, void* stream);
+int facek_edge_vec_bwd(int dtype, const void* dvec, const int32_t* row_ptr, const int32_t* rev, int64_t N,
+                       void* dpos, void* stream);
+int facek_edge_sym(int dtype, const void* vec, void* Y, int64_t E, void* stream);
+int facek_edge_sym_bwd(int dtype, const void* vec, const void* dY, void* dvec, int32_t accumulate, int64_t E,
+                       void* stream);
+
+/* Radial basis x learned radial MLP of one factorised block (face/model.py:28-40, :465-469):
+ * phi[e, b] = radial(silu(rad_in(bessel(r)*env(r)) + pair[zi*n_el + zj])) * env(r), and dphi/dr by forward-mode
+ * differentiation (replacing autograd through the MLP).  Weights are effective (unit scaling applied):
+ * w1 (H,nb) b1 (H) pair (n_el^2,H) w2 (H,H) b2 (H) w3 (B,H) b3 (B).
+ * Spline variant: cubic Hermite tables T, dT (n_el^2, G, B) on r = i*dr (face/model.py:383-418).
+ * radial_bwd: dvec[e] += u * sum_b dphi[e,b] * dphidr[e,b]. */
+int facek_radial_fwd(int dtype, const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx,
+                     int32_t n_el, double rc, int32_t nb, int32_t H, int32_t B, const void* w1, const void* b1,
+                     const void* pair, const void* w2, const void* b2, const void* w3, const void* b3, void* phi,
+                     void* dphidr, int64_t E, void* stream);
+int facek_radial_spline_fwd(int dtype, const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx,
+                            int32_t n_el, double rc, int32_t G, double dr, int32_t B, const void* T, const void* dT,
+                            void* phi, void* dphidr, int64_t E, void* stream);
+int facek_radial_bwd(int dtype, const void* vec, const void* dphi, const void* dphidr, int32_t B, void* dvec,
+                     int32_t accumulate, int64_t E, void* stream);
+
+/* Edge messages with directional terms (face/model.py:473-494), factorised as
+ * msg[e, k] = sum_{c<nc} Y[e, c] * (TJ[c, ej, k] + TI[c, ei, k])   (TI may be NULL),
+ * TJ/TI (nc, N, K) per-atom tables built from msg(h), dir_mix and the pvt/pmt projections.
+ * Backward: dY[e, c] (+)= ..., dTI (row-local sums) and dTJ (reverse gather), no atomics. */
+int facek_edge_msg_fwd(int dtype, const void* Y, const int32_t* ei, const int32_t* ej, const void* TJ,
+                       const void* TI, int32_t nc, int32_t K, void* msg, int64_t N, int64_t E, void* stream);
+int facek_edge_msg_bwd(int dtype, const void* Y, const int32_t* ei, const int32_t* ej, const void* TJ,
+                       const void* TI, const void* dmsg, const int32_t* row_ptr, const int32_t* rev, int32_t nc,
+                       int32_t K, void* dY, int32_t accumulate, void* dTJ, void* dTI, int64_t N, int64_t E,
+                       void* stream);
+
+/* Transport sums (face/model.py:514-533 with the constant maps :342-362) written per edge:
+ * T_o[i, b, kd] = sum_m phi[m,b] * f_o(u_m, Gt[:, ej_m, kd]),  f = [V | M u | M | sym(u (x) V)]  (18 outputs),
+ * Gt (9, N, Kd) = [V(3) | M sym(6)] of the transport channels.  DT holds two planes back to back:
+ * plane 1 (3, N, 2, B*Kd) = [V_a, (M u)_a] and plane 2 (6, N, 2, B*Kd) = [M_s, sym(u V)_s], so that
+ * (3, N, 2*B*Kd) and (6, N, 2*B*Kd) are the contiguous inputs of tmix1 / tmix2 (columns (t, b, kd)).
+ * Backward: the two plane gradients dT1, dT2; writes dphi (E,B), dvec (E,3) (+= when accumulate), and dGt via the
+ * per-edge scratch dGt_edge (E,9,Kd) reduced by the reverse gather. */
+int facek_transport_fwd(int dtype, const void* phi, const void* vec, const int32_t* ej, const void* Gt,
+                        const int32_t* row_ptr, void* DT, int64_t N, int32_t B, int32_t Kd, void* stream);
+int facek_transport_bwd(int dtype, const void* phi, const void* vec, const int32_t* ej, const void* Gt,
+                        const void* dT1, const void* dT2, const int32_t* row_ptr, const int32_t* rev, void* dphi,
+                        void* dvec, int32_t accumulate, void* dGt_edge, void* dGt, int64_t N, int64_t E, int32_t B,
+                        int32_t Kd, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Smooth PME (face-mlip face/electrostatics.py:34-77) and the Gaussian real-space term (:91-92, :125-127).
+ * inv: the 3x3 inverse cell (row-major, as torch.linalg.inv(cell)); mesh (n0*n1*n2) must be zeroed by the
+ * caller before spread.  spectrum: the half spectrum of rfftn(mesh), (n0, n1, n2/2+1) complex; green writes
+ * energy[0] += 1/(2V) sum_k G(k) B(k) |F(k)|^2 (accumulated in double; zero it first) and
+ * conv = G*B*F * (n0 n1 n2 / V) so that irfftn(conv) is the mesh potential dE/dQ.  bmod: |b(m)|^-2 per axis
+ * concatenated (n0 + n1 + n2).  gather: dq[i] = scale sum W phi, dpos[i] = scale q_i sum grad W phi.
+ * Real space: e_row[i] = 1/2 q_i sum_{e in row i} q_j K(r_e); the adjoint takes the per-row upstream g_row.
+ */
+int facek_pme_spread(int dtype, const void* pos, const void* q, int64_t N, const double* inv, int32_t n0,
+                     int32_t n1, int32_t n2, void* mesh, void* stream);
+int facek_pme_green(int dtype, const void* spectrum, int32_t n0, int32_t n1, int32_t n2, const double* inv,
+                    double gp, double volume, const void* bmod, double* energy, void* conv, void* stream);
+int facek_pme_gather(int dtype, const void* pos, const void* q, int64_t N, const double* inv, int32_t n0,
+                     int32_t n1, int32_t n2, const void* potential, double scale, void* dq, void* dpos,
+                     void* stream);
+int facek_coulomb_real_fwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej, const void* q,
+                           double gamma, double gp, int64_t N, void* e_row, void* stream);
+int facek_coulomb_real_bwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej, const void* q,
+                           double gamma, double gp, const void* g_row, int64_t N, void* dvec, int32_t accumulate,
+                           void* dq, void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+#endif
