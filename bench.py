@@ -174,7 +174,9 @@ def run_ours(a):
     dev = torch.device("cuda", 0)
     torch.cuda.set_device(dev)
     dtype = torch.float64 if a.config == 1 else torch.float32
-    structs, spec, pme = workload(a.config)
+    structs, spec, pme = workload(a.config, scale=a.scale)
+    if a.scale and a.config == 5:                           # keep the PME grid spacing of the full box
+        pme["mesh"] = tuple(max(8, int(round(n * a.scale / 64))) for n in pme["mesh"])
     model = make_model(spec, pme, dev, dtype)
     natoms = sum(len(s.numbers) for s in structs)
     g = build_graph(structs, spec["rc"], device=dev, dtype=dtype)
@@ -191,7 +193,8 @@ def run_ours(a):
     print(f"# warmup {a.warmup} steps {time.perf_counter() - t0:.2f} s, E={E} edges, peak mem "
           f"{torch.cuda.max_memory_allocated() / 2**30:.1f} GiB", file=sys.stderr, flush=True)
     # device-timed region: K steps, inputs resident in HBM (well above the 126 MB L2: edge tensors are GBs)
-    _lib.TIMED["facek_density_xm_fwd"] = []
+    for name in _lib.SIGNATURES:
+        _lib.TIMED[name] = []
     _lib.CALLS.clear()
     _lib.COUNTING = True
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -205,8 +208,9 @@ def run_ours(a):
     _lib.COUNTING = False
     launches = _lib.launches()
     ms = e0.elapsed_time(e1) / a.steps
-    dens = _lib.TIMED.pop("facek_density_xm_fwd")
-    dens_ms = [s.elapsed_time(t) for s, t in dens]
+    kernel_ms = {k[6:]: round(sum(s.elapsed_time(t) for s, t in v) / a.steps, 3) for k, v in _lib.TIMED.items() if v}
+    dens_ms = [s.elapsed_time(t) for s, t in _lib.TIMED["facek_density_xm_fwd"]]
+    _lib.TIMED.clear()
     value = natoms * a.steps / (e0.elapsed_time(e1) / 1e3)
     # density-kernel roofline: algorithmic bytes of one launch (phi, msg, Y per edge read; D per atom written)
     B, K = spec["B"], spec["K"]
@@ -245,7 +249,8 @@ def run_ours(a):
            "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
            "dtype": "f32" if dtype == torch.float32 else "f64", "data": "synthetic (seeded geometry, seeded random-init weights)",
            "config": {"workload": f"cfg{a.config}: " + ("1,048,576-atom fcc 5-element alloy, C64, 2 passes, PME 256^3"
-                                                         if a.config == 5 else f"BASELINE configuration {a.config}"),
+                                                         if a.config == 5 and not a.scale else
+                                                         f"BASELINE configuration {a.config}, scale {a.scale}"),
                       "atoms": natoms, "edges": E, "l2": "inputs larger than L2 (edge tensors of several GB)",
                       "parallelism": "single GPU"},
            "e2e": e2e,
@@ -253,7 +258,8 @@ def run_ours(a):
                         "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
                         "bytes_per_launch": bytes_launch, "launch_ms": t_launch * 1e3,
                         "peak_source": "measured" if "hbm_gbs" in pk else "fallback"},
-           "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches}
+           "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
+           "kernel_ms_per_step": kernel_ms}
     if rank == 0:
         print(json.dumps(out), flush=True)
 
@@ -282,6 +288,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--scale", type=int, default=None,
+                    help="smaller system of the same configuration (cfg5: conventional cells per side), for profiling")
     a = ap.parse_args()
     if a.impl == "reference":
         run_reference(a)

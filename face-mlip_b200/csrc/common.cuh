@@ -26,6 +26,32 @@ inline int grid_for(int64_t work_blocks, int per_sm) {
   return (int)(g < 1 ? 1 : g);
 }
 
+// ---- asynchronous global->shared copies (cp.async, 16-byte chunks; both addresses 16-byte aligned)
+__device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
+  const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));
+  asm volatile("cp.async.cg.shared.global [%0], [%1], 16;\n" ::"r"(s), "l"(gmem) : "memory");
+}
+__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;\n" ::: "memory"); }
+template <int N>
+__device__ __forceinline__ void cp_async_wait() {
+  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
+}
+
+// copy n elements of T from global to shared: cp.async in 16-byte chunks when both ends are 16-byte aligned
+// and n*sizeof(T) is a multiple of 16, else plain loads (caller syncs)
+template <typename T>
+__device__ __forceinline__ void stage(T* dst, const T* src, int n, int tid, int nthr) {
+  const bool vec = ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(src)) & 15) == 0 &&
+                   ((n * (int)sizeof(T)) & 15) == 0;
+  if (vec) {
+    const int nv = n * (int)sizeof(T) / 16;
+    for (int q = tid; q < nv; q += nthr) cp_async16(reinterpret_cast<char*>(dst) + 16 * q,
+                                                    reinterpret_cast<const char*>(src) + 16 * q);
+  } else {
+    for (int q = tid; q < n; q += nthr) dst[q] = src[q];
+  }
+}
+
 }  // namespace facek
 
 #define FACEK_CHECK_ARG(cond, ...)          \

@@ -47,146 +47,214 @@ struct Rows {
   }
 };
 
+// Forward.  The CTA walks its rows' edge tiles as one sequence and prefetches tile n+1 (possibly the next row's
+// first tile) with cp.async while tile n is consumed, so the staging latency is hidden behind the FMAs.
 template <typename T, int TB, int TK>
 __global__ void __launch_bounds__(256) dens_fwd_k(const T* __restrict__ phi, const T* __restrict__ msg,
                                                   const T* __restrict__ Y, Planes<T*> D, int64_t N, Rows rows,
                                                   int B, int K) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* sY = reinterpret_cast<T*>(smem_raw);        // FWD_TILE * 20
-  T* sP = sY + FWD_TILE * NX;                     // FWD_TILE * B
-  T* sM = sP + FWD_TILE * B;                      // FWD_TILE * K
+  const int tile_elems = FWD_TILE * (NX + B + K);
+  T* buf[2] = {reinterpret_cast<T*>(smem_raw), reinterpret_cast<T*>(smem_raw) + tile_elems};
   const int nb = B / TB, nk = K / TK;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int tb = tid / nk, tk = tid - (tid / nk) * nk;
   const bool active = tid < nb * nk;
   const int BK = B * K;
-  for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
-    int64_t e0;
-    int deg;
-    rows.range(i, e0, deg);
-    T acc[TB][TK][NX];
+  auto write_row = [&](int64_t i, T (*acc)[TK][NX]) {
+    if (!active) return;
 #pragma unroll
-    for (int a = 0; a < TB; a++)
+    for (int x = 0; x < NX; x++) {
+      T* out = D.at(i, x);
 #pragma unroll
-      for (int c = 0; c < TK; c++)
+      for (int a = 0; a < TB; a++)
 #pragma unroll
-        for (int x = 0; x < NX; x++) acc[a][c][x] = T(0);
-    for (int t0 = 0; t0 < deg; t0 += FWD_TILE) {
-      const int nt = min(FWD_TILE, deg - t0);
-      __syncthreads();
-      for (int q = tid; q < nt * NX; q += nthr) sY[q] = Y[(e0 + t0) * NX + q];
-      for (int q = tid; q < nt * B; q += nthr) sP[q] = phi[(e0 + t0) * B + q];
-      for (int q = tid; q < nt * K; q += nthr) sM[q] = msg[(e0 + t0) * K + q];
-      __syncthreads();
-      if (active) {
-        for (int t = 0; t < nt; t++) {
-          T y[NX];
+        for (int c = 0; c < TK; c++) out[(tb + a * nb) * K + tk + c * nk] = acc ? acc[a][c][x] : T(0);
+    }
+  };
+  // next (row, tile start) with edges, writing zero rows for empty rows on the way
+  auto advance = [&](int64_t& i, int& t0, int64_t& e0, int& deg) {
+    t0 += FWD_TILE;
+    if (t0 < deg) return;
+    t0 = 0;
+    for (i += gridDim.x; i < N; i += gridDim.x) {
+      rows.range(i, e0, deg);
+      if (deg > 0) return;
+      write_row(i, nullptr);
+    }
+  };
+  auto issue = [&](T* b, int64_t e0, int t0, int deg) {
+    const int nt = min(FWD_TILE, deg - t0);
+    T* sY = b;
+    T* sP = sY + FWD_TILE * NX;
+    T* sM = sP + FWD_TILE * B;
+    stage(sY, Y + (e0 + t0) * NX, nt * NX, tid, nthr);
+    stage(sP, phi + (e0 + t0) * B, nt * B, tid, nthr);
+    stage(sM, msg + (e0 + t0) * K, nt * K, tid, nthr);
+    cp_async_commit();
+  };
+  int64_t i = (int64_t)blockIdx.x - gridDim.x, e0 = 0;
+  int t0 = 0, deg = 0;
+  advance(i, t0, e0, deg);                      // first non-empty row (t0 = 0)
+  if (i < N) issue(buf[0], e0, t0, deg);
+  T acc[TB][TK][NX];
+#pragma unroll
+  for (int a = 0; a < TB; a++)
+#pragma unroll
+    for (int c = 0; c < TK; c++)
+#pragma unroll
+      for (int x = 0; x < NX; x++) acc[a][c][x] = T(0);
+  int cur = 0;
+  while (i < N) {
+    int64_t ni = i, ne0 = e0;
+    int nt0 = t0, ndeg = deg;
+    advance(ni, nt0, ne0, ndeg);
+    if (ni < N) {
+      issue(buf[cur ^ 1], ne0, nt0, ndeg);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const int nt = min(FWD_TILE, deg - t0);
+    const T* sY = buf[cur];
+    const T* sP = sY + FWD_TILE * NX;
+    const T* sM = sP + FWD_TILE * B;
+    if (active) {
+      for (int t = 0; t < nt; t++) {
+        T y[NX];
+        if constexpr (sizeof(T) == 4) {                // 5 x 128-bit broadcast loads (80-byte rows)
+          const float4* r4 = reinterpret_cast<const float4*>(sY + t * NX);
+#pragma unroll
+          for (int v = 0; v < NX / 4; v++) {
+            const float4 q = r4[v];
+            y[4 * v] = q.x; y[4 * v + 1] = q.y; y[4 * v + 2] = q.z; y[4 * v + 3] = q.w;
+          }
+        } else {
 #pragma unroll
           for (int x = 0; x < NX; x++) y[x] = sY[t * NX + x];
-          T p[TB], m[TK];
-#pragma unroll
-          for (int a = 0; a < TB; a++) p[a] = sP[t * B + tb + a * nb];
-#pragma unroll
-          for (int c = 0; c < TK; c++) m[c] = sM[t * K + tk + c * nk];
-#pragma unroll
-          for (int a = 0; a < TB; a++)
-#pragma unroll
-            for (int c = 0; c < TK; c++) {
-              const T w = p[a] * m[c];
-#pragma unroll
-              for (int x = 0; x < NX; x++) acc[a][c][x] += w * y[x];
-            }
         }
-      }
-    }
-    if (active) {
+        T p[TB], m[TK];
 #pragma unroll
-      for (int x = 0; x < NX; x++) {
-        T* out = D.at(i, x);
+        for (int a = 0; a < TB; a++) p[a] = sP[t * B + tb + a * nb];
+#pragma unroll
+        for (int c = 0; c < TK; c++) m[c] = sM[t * K + tk + c * nk];
 #pragma unroll
         for (int a = 0; a < TB; a++)
 #pragma unroll
-          for (int c = 0; c < TK; c++) out[(tb + a * nb) * K + tk + c * nk] = acc[a][c][x];
+          for (int c = 0; c < TK; c++) {
+            const T w = p[a] * m[c];
+#pragma unroll
+            for (int x = 0; x < NX; x++) acc[a][c][x] += w * y[x];
+          }
       }
     }
+    if (t0 + FWD_TILE >= deg) {                 // row complete
+      write_row(i, acc);
+#pragma unroll
+      for (int a = 0; a < TB; a++)
+#pragma unroll
+        for (int c = 0; c < TK; c++)
+#pragma unroll
+          for (int x = 0; x < NX; x++) acc[a][c][x] = T(0);
+    }
+    __syncthreads();                            // buf[cur] is refilled two tiles from now
+    i = ni; e0 = ne0; t0 = nt0; deg = ndeg;
+    cur ^= 1;
   }
 }
 
-template <typename T, int BMAX, int KC>
-__global__ void __launch_bounds__(128) dens_bwd_k(const T* __restrict__ phi, const T* __restrict__ msg,
+// Backward.  One CTA per row at a time; the row's G (20 x BK, as laid out in global: [x][bk]) sits in shared memory
+// and the next row's G is prefetched with cp.async into the other buffer.  Each edge is handled by KS threads, one
+// k-chunk of KC channels each, walking (b, k) in lockstep so every G read is a broadcast.  The 20-term dot products
+// use four partial sums (independent FMA chains).
+template <typename T, int KC, int BMAX>
+__global__ void __launch_bounds__(256) dens_bwd_k(const T* __restrict__ phi, const T* __restrict__ msg,
                                                   const T* __restrict__ Y, Planes<const T*> G,
                                                   T* __restrict__ dphi, T* __restrict__ dmsg, T* __restrict__ dY,
                                                   int64_t N, Rows rows, int B, int K, int KS) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* sG = reinterpret_cast<T*>(smem_raw);   // (B*K) x 20, x fastest
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int BK = B * K;
+  T* sGb[2] = {reinterpret_cast<T*>(smem_raw), reinterpret_cast<T*>(smem_raw) + NX * BK};
   const int kc = tid % KS;                  // this thread's k chunk
   const int slot = tid / KS;                // edge slot within a pass
   const int per_pass = nthr / KS;
   const int k0 = kc * KC;
+  auto issue = [&](T* sG, int64_t i) {
+#pragma unroll 4
+    for (int x = 0; x < NX; x++) stage(sG + x * BK, G.at(i, x), BK, tid, nthr);
+    cp_async_commit();
+  };
+  int cur = 0;
+  if ((int64_t)blockIdx.x < N) issue(sGb[0], blockIdx.x);
   for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
+    const int64_t inext = i + gridDim.x;
+    if (inext < N) {
+      issue(sGb[cur ^ 1], inext);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
+    }
+    __syncthreads();
+    const T* sG = sGb[cur];
     int64_t e0;
     int deg;
     rows.range(i, e0, deg);
-    __syncthreads();
-    for (int q = tid; q < NX * BK; q += nthr) {     // coalesced read of [x][bk], transposed store
-      const int x = q / BK, c = q - x * BK;
-      sG[c * NX + x] = G.at(i, x)[c];
-    }
-    __syncthreads();
     for (int t0 = 0; t0 < deg; t0 += per_pass) {
       const int t = t0 + slot;
-      const bool live = t < deg && slot < per_pass;
+      const bool live = t < deg;
       const int64_t e = e0 + (live ? t : 0);
-      T y[NX], dy[NX], p[BMAX], dp[BMAX], m[KC], dm[KC];
+      T y[NX], dy[NX], m[KC], dm[KC];
 #pragma unroll
       for (int x = 0; x < NX; x++) { y[x] = live ? Y[e * NX + x] : T(0); dy[x] = T(0); }
 #pragma unroll
-      for (int b = 0; b < BMAX; b++) { p[b] = (live && b < B) ? phi[e * B + b] : T(0); dp[b] = T(0); }
-#pragma unroll
       for (int c = 0; c < KC; c++) { m[c] = (live && k0 + c < K) ? msg[e * K + k0 + c] : T(0); dm[c] = T(0); }
+      T pnext = live ? phi[e * B] : T(0);         // phi_b is loaded one b ahead (hides the load latency)
+      for (int b = 0; b < B; b++) {
+        const T pb = pnext;
+        if (b + 1 < B) pnext = live ? phi[e * B + b + 1] : T(0);
+        T dpb = 0;
 #pragma unroll
-      for (int b = 0; b < BMAX; b++) {
-        if (b < B) {
+        for (int c = 0; c < KC; c++) {
+          const int k = k0 + c < K ? k0 + c : K - 1;
+          const T* gg = sG + b * K + k;
+          T gx[NX];
 #pragma unroll
-          for (int c = 0; c < KC; c++) {
-            const int k = k0 + c < K ? k0 + c : K - 1;
-            const T* gg = sG + (b * K + k) * NX;
-            T gx[NX];
+          for (int x = 0; x < NX; x++) gx[x] = gg[x * BK];
+          T s0 = 0, s1 = 0, s2 = 0, s3 = 0;
 #pragma unroll
-            for (int x = 0; x < NX; x++) gx[x] = gg[x];
-            T s = 0;
-#pragma unroll
-            for (int x = 0; x < NX; x++) s += gx[x] * y[x];
-            dp[b] += s * m[c];
-            dm[c] += s * p[b];
-            const T w = p[b] * m[c];
-#pragma unroll
-            for (int x = 0; x < NX; x++) dy[x] += gx[x] * w;
+          for (int x = 0; x < NX; x += 4) {
+            s0 += gx[x] * y[x];
+            s1 += gx[x + 1] * y[x + 1];
+            s2 += gx[x + 2] * y[x + 2];
+            s3 += gx[x + 3] * y[x + 3];
           }
-        }
-      }
-      // reduce the k-chunk partials of dphi and dY across the KS threads of this edge
-      for (int off = 1; off < KS; off <<= 1) {
+          const T s = (s0 + s1) + (s2 + s3);
+          dpb += s * m[c];
+          dm[c] += s * pb;
+          const T w = pb * m[c];
 #pragma unroll
-        for (int b = 0; b < BMAX; b++) dp[b] += __shfl_xor_sync(0xffffffffu, dp[b], off);
+          for (int x = 0; x < NX; x++) dy[x] += gx[x] * w;
+        }
+        for (int off = 1; off < KS; off <<= 1) dpb += __shfl_xor_sync(0xffffffffu, dpb, off);
+        if (live && kc == 0) dphi[e * B + b] = dpb;
+      }
+      for (int off = 1; off < KS; off <<= 1)
 #pragma unroll
         for (int x = 0; x < NX; x++) dy[x] += __shfl_xor_sync(0xffffffffu, dy[x], off);
-      }
       if (live) {
 #pragma unroll
         for (int c = 0; c < KC; c++)
           if (k0 + c < K) dmsg[e * K + k0 + c] = dm[c];
         if (kc == 0) {
 #pragma unroll
-          for (int b = 0; b < BMAX; b++)
-            if (b < B) dphi[e * B + b] = dp[b];
-#pragma unroll
           for (int x = 0; x < NX; x++) dY[e * NX + x] = dy[x];
         }
       }
     }
+    __syncthreads();                          // sG[cur] is refilled next iteration
+    cur ^= 1;
   }
 }
 
@@ -195,8 +263,8 @@ int launch_fwd(const void* phi, const void* msg, const void* Y, Planes<T*> D, in
                void* stream) {
   const int threads = (B / TB) * (K / TK);
   const int threads_r = ceil_div(threads, 32) * 32;
-  const size_t smem = sizeof(T) * FWD_TILE * (NX + B + K);
-  const int grid = grid_for(N, 8);
+  const size_t smem = 2 * sizeof(T) * FWD_TILE * (NX + B + K);
+  const int grid = grid_for(N, 6);
   dens_fwd_k<T, TB, TK><<<grid, threads_r, smem, as_stream(stream)>>>((const T*)phi, (const T*)msg, (const T*)Y,
                                                                      D, N, rows, B, K);
   return launch_status("facek_density_fwd");
@@ -217,21 +285,21 @@ int density_fwd(const void* phi, const void* msg, const void* Y, Planes<T*> D, i
   return launch_fwd<T, 1, 1>(phi, msg, Y, D, N, rows, B, K, stream);
 }
 
-template <typename T, int BMAX, int KC>
+template <typename T, int KC, int BMAX>
 int launch_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*> G, void* dphi, void* dmsg,
                void* dY, int64_t N, Rows rows, int B, int K, void* stream) {
   int KS = ceil_div(K, KC);
   int ks2 = 1;
   while (ks2 < KS) ks2 <<= 1;                     // shuffle groups are powers of two
   FACEK_CHECK_ARG(ks2 <= 32, "facek_density_bwd: K=%d too large", K);
-  const size_t smem = sizeof(T) * (size_t)B * K * NX;
-  if (smem > 48 * 1024) {
-    FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_density_bwd: G tile %zu B exceeds shared memory", smem);
-    cudaFuncSetAttribute(dens_bwd_k<T, BMAX, KC>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-  }
-  const int grid = grid_for(N, 4);
-  dens_bwd_k<T, BMAX, KC><<<grid, 128, smem, as_stream(stream)>>>((const T*)phi, (const T*)msg, (const T*)Y,
-                                                                  G, (T*)dphi, (T*)dmsg, (T*)dY, N, rows, B, K, ks2);
+  const int threads = ks2 * 48 <= 256 ? ks2 * 48 : 256;   // 48 edge slots per pass (rows of ~45 edges)
+  const size_t smem = 2 * sizeof(T) * (size_t)B * K * NX;
+  FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_density_bwd: G tiles %zu B exceed shared memory", smem);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(dens_bwd_k<T, KC, BMAX>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  const int grid = grid_for(N, 2);
+  dens_bwd_k<T, KC, BMAX><<<grid, threads, smem, as_stream(stream)>>>((const T*)phi, (const T*)msg, (const T*)Y, G,
+                                                                (T*)dphi, (T*)dmsg, (T*)dY, N, rows, B, K, ks2);
   return launch_status("facek_density_bwd");
 }
 
@@ -242,11 +310,11 @@ int density_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*
   Rows rows{row_ptr, M};
   FACEK_CHECK_ARG(B <= 32, "facek_density_bwd: B=%d > 32 unsupported", B);
   if constexpr (sizeof(T) == 4) {
-    if (B <= 16) return launch_bwd<T, 16, 16>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
-    return launch_bwd<T, 32, 8>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
+    if (B <= 16) return launch_bwd<T, 8, 16>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
+    return launch_bwd<T, 8, 32>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
   } else {
-    if (B <= 16) return launch_bwd<T, 16, 4>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
-    return launch_bwd<T, 32, 4>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
+    if (B <= 16) return launch_bwd<T, 4, 16>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
+    return launch_bwd<T, 4, 32>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
   }
 }
 

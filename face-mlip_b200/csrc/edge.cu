@@ -190,23 +190,37 @@ __global__ void __launch_bounds__(128) radial_mlp_k(const T* __restrict__ vec, c
     T z3[BMAX], dz3[BMAX];
 #pragma unroll
     for (int b = 0; b < BMAX; b++) { z3[b] = 0; dz3[b] = 0; }
-    for (int o = 0; o < H; o++) {
-      const T* w = sW2 + o * H;
-      T z = sB2[o], dz = 0;
+    // layer 2 four output neurons at a time: 8 independent FMA chains, weights read as broadcasts
+    for (int o0 = 0; o0 < H; o0 += 4) {
+      T z[4], dz[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        z[j] = (o0 + j < H) ? sB2[o0 + j] : T(0);
+        dz[j] = 0;
+      }
 #pragma unroll
       for (int h = 0; h < HMAX; h++)
         if (h < H) {
-          z += w[h] * a1[h];
-          dz += w[h] * da1[h];
-        }
-      const T s = sigmoid(z);
-      const T a2 = z * s, da2 = s * (T(1) + z * (T(1) - s)) * dz;
 #pragma unroll
-      for (int b = 0; b < BMAX; b++)
-        if (b < B) {
-          z3[b] += sW3[b * H + o] * a2;
-          dz3[b] += sW3[b * H + o] * da2;
+          for (int j = 0; j < 4; j++) {
+            const T w = (o0 + j < H) ? sW2[(o0 + j) * H + h] : T(0);
+            z[j] += w * a1[h];
+            dz[j] += w * da1[h];
+          }
         }
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        if (o0 + j < H) {
+          const T sg = sigmoid(z[j]);
+          const T a2 = z[j] * sg, da2 = sg * (T(1) + z[j] * (T(1) - sg)) * dz[j];
+#pragma unroll
+          for (int b = 0; b < BMAX; b++)
+            if (b < B) {
+              z3[b] += sW3[b * H + o0 + j] * a2;
+              dz3[b] += sW3[b * H + o0 + j] * da2;
+            }
+        }
+      }
     }
 #pragma unroll
     for (int b = 0; b < BMAX; b++)
@@ -464,29 +478,42 @@ __global__ void __launch_bounds__(256) transport_fwd_k(const T* __restrict__ phi
   }
 }
 
-// CTA per row with dDT staged in shared memory; each edge handled by Kd/4 threads (4 kd channels each)
+// CTA per row with the row's 18 gradient rows (dT1/dT2 planes) staged in shared memory by cp.async, the next row
+// prefetched into the second buffer; each edge is handled by KQ threads (KDT = 2 kd channels each).
 template <typename T, int BMAX>
-__global__ void __launch_bounds__(128) transport_bwd_k(const T* __restrict__ phi, const T* __restrict__ vec,
+__global__ void __launch_bounds__(256) transport_bwd_k(const T* __restrict__ phi, const T* __restrict__ vec,
                                                        const int32_t* __restrict__ ej, const T* __restrict__ Gt,
                                                        const T* __restrict__ dT1, const T* __restrict__ dT2,
                                                        const int32_t* __restrict__ row_ptr,
                                                        T* __restrict__ dphi, T* __restrict__ dvec, int acc,
                                                        T* __restrict__ dGe, int64_t N, int B, int Kd, int KQ) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
-  T* sD = reinterpret_cast<T*>(smem_raw);   // 18 x B*Kd
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int BKd = B * Kd;
+  T* sDb[2] = {reinterpret_cast<T*>(smem_raw), reinterpret_cast<T*>(smem_raw) + 18 * BKd};
   const int kq = tid % KQ, slot = tid / KQ, per_pass = nthr / KQ;
-  for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
-    const int64_t e0 = row_ptr[i];
-    const int deg = row_ptr[i + 1] - row_ptr[i];
-    __syncthreads();
-    for (int q = tid; q < 18 * BKd; q += nthr) {
-      const int r = q / BKd, c = q - r * BKd;
+  auto issue = [&](T* sD, int64_t i) {
+#pragma unroll 2
+    for (int r = 0; r < 18; r++) {
       const int64_t off = plane_off(r, i, N, BKd);
-      sD[q] = r < 6 ? dT1[off + c] : dT2[off - 6 * N * (int64_t)BKd + c];
+      stage(sD + r * BKd, r < 6 ? dT1 + off : dT2 + (off - 6 * N * (int64_t)BKd), BKd, tid, nthr);
+    }
+    cp_async_commit();
+  };
+  int cur = 0;
+  if ((int64_t)blockIdx.x < N) issue(sDb[0], blockIdx.x);
+  for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
+    const int64_t inext = i + gridDim.x;
+    if (inext < N) {
+      issue(sDb[cur ^ 1], inext);
+      cp_async_wait<1>();
+    } else {
+      cp_async_wait<0>();
     }
     __syncthreads();
+    const T* sD = sDb[cur];
+    const int64_t e0 = row_ptr[i];
+    const int deg = row_ptr[i + 1] - row_ptr[i];
     for (int t0 = 0; t0 < deg; t0 += per_pass) {
       const int t = t0 + slot;
       const bool live = t < deg;
@@ -494,46 +521,45 @@ __global__ void __launch_bounds__(128) transport_bwd_k(const T* __restrict__ phi
       const T vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
       const T r = sqrt(vx * vx + vy * vy + vz * vz);
       const T u[3] = {vx / r, vy / r, vz / r};
-      T p[BMAX], dp[BMAX];
-#pragma unroll
-      for (int b = 0; b < BMAX; b++) { p[b] = (live && b < B) ? phi[e * B + b] : T(0); dp[b] = 0; }
-      T g[4][9], f[4][18], Pd[4][18];
+      constexpr int KDT = 2;
+      T f[KDT][18], Pd[KDT][18];
       const T* gj = Gt + (int64_t)ej[e] * Kd;
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        const int k = kq * 4 + q;
+      for (int q = 0; q < KDT; q++) {
+        const int k = kq * KDT + q;
+        T g[9];
 #pragma unroll
-        for (int c = 0; c < 9; c++) g[q][c] = k < Kd ? gj[c * N * Kd + k] : T(0);
-        transport_f(u[0], u[1], u[2], g[q], f[q]);
+        for (int c = 0; c < 9; c++) g[c] = k < Kd ? gj[c * N * Kd + k] : T(0);
+        transport_f(u[0], u[1], u[2], g, f[q]);
 #pragma unroll
         for (int o = 0; o < 18; o++) Pd[q][o] = 0;
       }
+      // b outer (runtime), the 18 outputs unrolled: phi_b and its gradient stay scalars
+      for (int b = 0; b < B; b++) {
+        const T pb = live ? phi[e * B + b] : T(0);
+        T dpb = 0;
+        const T* rowb = sD + b * Kd + kq * KDT;
 #pragma unroll
-      for (int o = 0; o < 18; o++) {
-        const T* row = sD + (int64_t)trow(o) * BKd + kq * 4;
+        for (int o = 0; o < 18; o++) {
+          const T* row = rowb + (int64_t)trow(o) * BKd;
+          T d2[KDT];
 #pragma unroll
-        for (int b = 0; b < BMAX; b++) {
-          if (b < B) {
-            T d4[4];
+          for (int q = 0; q < KDT; q++) d2[q] = (kq * KDT + q < Kd) ? row[q] : T(0);
+          dpb += d2[0] * f[0][o] + d2[1] * f[1][o];
 #pragma unroll
-            for (int q = 0; q < 4; q++) d4[q] = (kq * 4 + q < Kd) ? row[b * Kd + q] : T(0);
-#pragma unroll
-            for (int q = 0; q < 4; q++) {
-              Pd[q][o] += p[b] * d4[q];
-              dp[b] += d4[q] * f[q][o];
-            }
-          }
+          for (int q = 0; q < KDT; q++) Pd[q][o] += pb * d2[q];
         }
+        for (int off = 1; off < KQ; off <<= 1) dpb += __shfl_xor_sync(0xffffffffu, dpb, off);
+        if (live && kq == 0) dphi[e * B + b] = dpb;
       }
-      // dphi: reduce over the KQ threads of this edge
-      for (int off = 1; off < KQ; off <<= 1)
-#pragma unroll
-        for (int b = 0; b < BMAX; b++) dp[b] += __shfl_xor_sync(0xffffffffu, dp[b], off);
       // adjoint of f -> dV, dMs (per kd) and du
       T du[3] = {0, 0, 0};
 #pragma unroll
-      for (int q = 0; q < 4; q++) {
-        T dV[3], dM[6];
+      for (int q = 0; q < KDT; q++) {
+        T dV[3], dM[6], g[9];
+        const int kk = kq * KDT + q;
+#pragma unroll
+        for (int c = 0; c < 9; c++) g[c] = kk < Kd ? gj[c * N * Kd + kk] : T(0);     // reload (L1/L2 hit)
 #pragma unroll
         for (int a = 0; a < 3; a++) dV[a] = Pd[q][a];
 #pragma unroll
@@ -543,23 +569,23 @@ __global__ void __launch_bounds__(128) transport_bwd_k(const T* __restrict__ phi
 #pragma unroll
           for (int b = 0; b < 3; b++) {
             dM[s2i(a, b)] += Pd[q][3 + a] * u[b];
-            du[b] += Pd[q][3 + a] * g[q][3 + s2i(a, b)];
+            du[b] += Pd[q][3 + a] * g[3 + s2i(a, b)];
           }
 #pragma unroll
         for (int s = 0; s < 6; s++) {
           const int pp = pair_p(s), qq = pair_q(s);
           const T w = Pd[q][12 + s];
           if (pp == qq) {
-            du[pp] += w * g[q][pp];
+            du[pp] += w * g[pp];
             dV[pp] += w * u[pp];
           } else {
-            du[pp] += T(0.5) * w * g[q][qq];
-            du[qq] += T(0.5) * w * g[q][pp];
+            du[pp] += T(0.5) * w * g[qq];
+            du[qq] += T(0.5) * w * g[pp];
             dV[qq] += T(0.5) * w * u[pp];
             dV[pp] += T(0.5) * w * u[qq];
           }
         }
-        const int k = kq * 4 + q;
+        const int k = kq * KDT + q;
         if (live && k < Kd) {
           T* dg = dGe + e * 9 * (int64_t)Kd + k;
 #pragma unroll
@@ -572,9 +598,6 @@ __global__ void __launch_bounds__(128) transport_bwd_k(const T* __restrict__ phi
 #pragma unroll
         for (int d = 0; d < 3; d++) du[d] += __shfl_xor_sync(0xffffffffu, du[d], off);
       if (live && kq == 0) {
-#pragma unroll
-        for (int b = 0; b < BMAX; b++)
-          if (b < B) dphi[e * B + b] = dp[b];
         T dx, dy, dz;
         unit_bwd(u[0], u[1], u[2], r, du[0], du[1], du[2], dx, dy, dz);
         if (acc) {
@@ -584,6 +607,8 @@ __global__ void __launch_bounds__(128) transport_bwd_k(const T* __restrict__ phi
         }
       }
     }
+    __syncthreads();
+    cur ^= 1;
   }
 }
 
@@ -728,23 +753,24 @@ int transport_bwd(const void* phi, const void* vec, const int32_t* ej, const voi
                   void* dGe, void* dGt, int64_t N, int64_t E, int B, int Kd, void* stream) {
   if (N == 0) return FACEK_OK;
   int KQ = 1;
-  while (KQ * 4 < Kd) KQ <<= 1;
+  while (KQ * 2 < Kd) KQ <<= 1;                   // two kd channels per thread
   FACEK_CHECK_ARG(KQ <= 32, "facek_transport_bwd: Kd=%d too large", Kd);
-  const size_t smem = sizeof(T) * 18 * (size_t)B * Kd;
-  FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_transport_bwd: gradient tile %zu B exceeds shared memory",
+  const size_t smem = 2 * sizeof(T) * 18 * (size_t)B * Kd;
+  FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_transport_bwd: gradient tiles %zu B exceed shared memory",
                   smem);
+  const int threads = KQ * 32 <= 256 ? KQ * 32 : 256;   // 32 edge slots per pass
   if (E > 0) {
     if (B <= 16) {
       if (smem > 48 * 1024)
         cudaFuncSetAttribute(transport_bwd_k<T, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      transport_bwd_k<T, 16><<<grid_for(N, 4), 128, smem, as_stream(stream)>>>(
+      transport_bwd_k<T, 16><<<grid_for(N, 2), threads, smem, as_stream(stream)>>>(
           (const T*)phi, (const T*)vec, ej, (const T*)Gt, (const T*)dT1, (const T*)dT2, row_ptr, (T*)dphi, (T*)dvec,
           acc, (T*)dGe, N, B, Kd, KQ);
     } else {
       FACEK_CHECK_ARG(B <= 32, "facek_transport_bwd: B=%d > 32", B);
       if (smem > 48 * 1024)
         cudaFuncSetAttribute(transport_bwd_k<T, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      transport_bwd_k<T, 32><<<grid_for(N, 4), 128, smem, as_stream(stream)>>>(
+      transport_bwd_k<T, 32><<<grid_for(N, 2), threads, smem, as_stream(stream)>>>(
           (const T*)phi, (const T*)vec, ej, (const T*)Gt, (const T*)dT1, (const T*)dT2, row_ptr, (T*)dphi, (T*)dvec,
           acc, (T*)dGe, N, B, Kd, KQ);
     }

@@ -468,6 +468,21 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
     return o[:, 0], h + o[:, 1:], A, eq_new
 
 
+def seg_sum(x, batch, nstr):
+    """Per-structure sums; a plain reduction when the batch holds one structure (an index_add of N atoms into one
+    element serialises on atomics)."""
+    if nstr == 1:
+        return x.sum(0, keepdim=True)
+    return torch.zeros(nstr, *x.shape[1:], dtype=x.dtype, device=x.device).index_add(0, batch, x)
+
+
+def per_atom(v, batch, nstr):
+    """Broadcast per-structure values to atoms (expand, whose adjoint is a reduction, for a single structure)."""
+    if nstr == 1:
+        return v.expand(batch.shape[0], *v.shape[1:])
+    return v[batch]
+
+
 def coulomb_term(P, gr, geo, h, pos):
     """LatentCharges.forward, mode 'local' (face/electrostatics.py:132-176)."""
     c = P["coulomb"]
@@ -475,11 +490,11 @@ def coulomb_term(P, gr, geo, h, pos):
     J = F.softplus(hard) + 0.1
     batch, nstr = gr["batch"], gr["nstr"]
     invJ = 1.0 / J
-    num = torch.zeros(nstr, dtype=chi.dtype, device=chi.device).index_add(0, batch, chi * invJ)
-    den = torch.zeros(nstr, dtype=chi.dtype, device=chi.device).index_add(0, batch, invJ)
+    num = seg_sum(chi * invJ, batch, nstr)
+    den = seg_sum(invJ, batch, nstr)
     Q = gr["charge"].to(chi.dtype)
     mu = (Q + num) / den
-    q = -(chi - mu[batch]) * invJ
+    q = -(chi - per_atom(mu, batch, nstr)) * invJ
     gamma, gp = c["gamma"], c["gp"]
     natoms = gr["natoms"]
     if not all(gr["pbc"]):
@@ -491,9 +506,9 @@ def coulomb_term(P, gr, geo, h, pos):
         A = torch.where(same, torch.erf(d / gamma) / d, torch.zeros_like(d))
         return chi * q + 0.5 * J * q * q + 0.5 * KE * q * (A @ q), q
     e_row = CoulombReal.apply(geo["vec"], q, gr, gamma, gp)
-    e_real = torch.zeros(nstr, dtype=q.dtype, device=q.device).index_add(0, batch, e_row)
-    q2 = torch.zeros(nstr, dtype=q.dtype, device=q.device).index_add(0, batch, q * q)
-    qs = torch.zeros(nstr, dtype=q.dtype, device=q.device).index_add(0, batch, q)
+    e_real = seg_sum(e_row, batch, nstr)
+    q2 = seg_sum(q * q, batch, nstr)
+    qs = seg_sum(q, batch, nstr)
     e_recip = []
     offs = [0] + np.cumsum(natoms.tolist()).tolist()
     for s in range(nstr):
@@ -507,7 +522,7 @@ def coulomb_term(P, gr, geo, h, pos):
     e_recip = torch.stack(e_recip)
     vol = torch.as_tensor([abs(np.linalg.det(gr["cell64"][s])) for s in range(nstr)], dtype=q.dtype, device=q.device)
     e_es = KE * (e_recip + e_real - q2 / (math.sqrt(math.pi) * gp) - 0.5 * math.pi * gp ** 2 / vol * qs ** 2)
-    return chi * q + 0.5 * J * q * q + (e_es / natoms.to(q.dtype))[batch], q
+    return chi * q + 0.5 * J * q * q + per_atom(e_es / natoms.to(q.dtype), batch, nstr), q
 
 
 def face_forward(model, g, forces=True):
@@ -541,7 +556,7 @@ def face_forward(model, g, forces=True):
         if "coulomb" in P:
             ea, qv = coulomb_term(P, gr, geo, h, pos)
             e_at = e_at + ea
-        E = torch.zeros(gr["nstr"], dtype=e_at.dtype, device=dev).index_add(0, gr["batch"], e_at)
+        E = seg_sum(e_at, gr["batch"], gr["nstr"])
         out = {"energy": E.detach(), "atom_energy": e_at.detach()}
         if qv is not None:
             out["q"] = qv.detach()
