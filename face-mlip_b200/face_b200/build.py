@@ -64,7 +64,7 @@ def build(verbose=False, ptxas=False, force=False):
         if verbose or ptxas:
             sys.stderr.write(r.stderr)
     tmp = LIB + ".tmp"
-    cmd = [nvcc(), *ARCH, "-shared", *[o for _, o, _ in results], "-lcufft", "-o", tmp]
+    cmd = [nvcc(), *ARCH, "-shared", *[o for _, o, _ in results], "-o", tmp]
     if verbose:
         print(" ".join(cmd), flush=True)
     r = subprocess.run(cmd, capture_output=True, text=True)
