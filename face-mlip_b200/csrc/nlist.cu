@@ -11,6 +11,8 @@
 // along each lattice plane normal; each atom scans (2ns+1)^3 cells, cell images giving the shift S.  Cell
 // contents are sorted by atom index, the per-row output is sorted by key, so the result is deterministic.
 // Non-periodic batches: all pairs inside each structure (molecules of tens of atoms).
+#include <mutex>
+
 #include "common.cuh"
 
 namespace facek {
@@ -353,6 +355,97 @@ int batch_fill(const double* pos, int64_t N, const int32_t* sstart, const int32_
   return launch_status("facek_nlist_batch_fill");
 }
 
+// ---------------------------------------------------------------------------------------------------------------
+// Allocation-free variant of the periodic build.  Its scratch (cell counts and offsets, per-atom bin and wrap, the
+// cell-sorted atom order, per-atom degrees) lives in one file-scope device array instead of a caller buffer, for
+// callers that cannot allocate device memory.  Limits: NOALLOC_MAX_ATOMS atoms, NOALLOC_MAX_CELLS cells.
+constexpr int64_t NOALLOC_MAX_ATOMS = 262144;
+constexpr int64_t NOALLOC_MAX_CELLS = 65536;
+constexpr int64_t NOALLOC_INTS = 3 * NOALLOC_MAX_CELLS + 1 + 5 * NOALLOC_MAX_ATOMS + 1 + NOALLOC_MAX_ATOMS;
+
+static __device__ __align__(256) int g_nlist_scratch[NOALLOC_INTS];     // about 7.1 MB per device
+
+// Device address of the scratch array for the current device: g_nlist_scratch named in host code is only a
+// host-side stand-in, so the address is looked up once per device with that device current.
+int noalloc_scratch(int** out) {
+  static std::mutex mu;
+  static int* addr[128] = {nullptr};
+  int dev = 0;
+  cudaError_t e = cudaGetDevice(&dev);
+  if (e != cudaSuccess || dev < 0 || dev >= 128) {
+    set_error("facek_nlist_cell_build_noalloc: cudaGetDevice failed (%s)", cudaGetErrorString(e));
+    return FACEK_ELAUNCH;
+  }
+  std::lock_guard<std::mutex> lock(mu);
+  if (!addr[dev]) {
+    void* p = nullptr;
+    e = cudaGetSymbolAddress(&p, g_nlist_scratch);
+    if (e != cudaSuccess || !p) {
+      set_error("facek_nlist_cell_build_noalloc: cudaGetSymbolAddress failed (%s)", cudaGetErrorString(e));
+      return FACEK_ELAUNCH;
+    }
+    addr[dev] = static_cast<int*>(p);
+  }
+  *out = addr[dev];
+  return FACEK_OK;
+}
+
+template <typename T>
+int build_noalloc(const double* pos, int64_t N, const double* cell, double rc, int64_t max_edges, int32_t* row_ptr,
+                  int32_t* ei, int32_t* ej, int32_t* S, void* shift, int64_t* n_edges, void* stream) {
+  CellGrid g;
+  int st = make_grid(cell, rc, g);
+  if (st) return st;
+  FACEK_CHECK_ARG(N <= NOALLOC_MAX_ATOMS, "facek_nlist_cell_build_noalloc: N=%lld atoms exceeds the limit of %lld",
+                  (long long)N, (long long)NOALLOC_MAX_ATOMS);
+  FACEK_CHECK_ARG(g.ncells <= NOALLOC_MAX_CELLS,
+                  "facek_nlist_cell_build_noalloc: %lld cells exceed the limit of %lld (cell too large for rc)",
+                  (long long)g.ncells, (long long)NOALLOC_MAX_CELLS);
+  int* scratch = nullptr;
+  st = noalloc_scratch(&scratch);
+  if (st) return st;
+  cudaStream_t s = as_stream(stream);
+  const int64_t used = ws_ints(N, g.ncells);
+  Work w = carve(scratch, N, g.ncells);
+  int32_t* deg = scratch + used;
+  // the array keeps the previous call's contents: clear every counter this call relies on
+  if (cudaMemsetAsync(scratch, 0, sizeof(int) * (used + N), s) != cudaSuccess) return launch_status("memset");
+  bin_k<<<ew_grid(N), 128, 0, s>>>(pos, N, g, w);
+  scan_k<<<1, 1024, 0, s>>>(w.count, w.start, g.ncells);
+  scatter_k<<<ew_grid(N), 128, 0, s>>>(N, w);
+  sort_cells_k<<<ew_grid(g.ncells), 128, 0, s>>>(g.ncells, w);
+  cell_rows_k<false, float><<<ew_grid(N), 128, 0, s>>>(pos, N, g, w, rc, deg, nullptr, nullptr, nullptr, nullptr,
+                                                        nullptr);
+  scan_k<<<1, 1024, 0, s>>>(deg, row_ptr, N);
+  st = launch_status("facek_nlist_cell_build_noalloc(count)");
+  if (st) return st;
+  int total = 0;
+  cudaMemcpyAsync(&total, row_ptr + N, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return launch_status("facek_nlist_cell_build_noalloc(sync)");
+  *n_edges = total;
+  if (total > max_edges) {
+    set_error("facek_nlist_cell_build_noalloc: %d edges exceed the output capacity max_edges=%lld", total,
+              (long long)max_edges);
+    return FACEK_EINVAL;
+  }
+  if (total == 0) return FACEK_OK;
+  cell_rows_k<true, T><<<ew_grid(N), 128, 0, s>>>(pos, N, g, w, rc, nullptr, row_ptr, ei, ej, S, (T*)shift);
+  st = launch_status("facek_nlist_cell_build_noalloc(fill)");
+  if (st) return st;
+  int flag = 0;
+  cudaMemcpyAsync(&flag, w.flag, sizeof(int), cudaMemcpyDeviceToHost, s);
+  if (cudaStreamSynchronize(s) != cudaSuccess) return launch_status("facek_nlist_cell_build_noalloc(sync)");
+  if (flag == 1) {
+    set_error("facek_nlist_cell_build_noalloc: a row has more than %d neighbours", MAXDEG);
+    return FACEK_EUNSUPPORTED;
+  }
+  if (flag == 2) {
+    set_error("facek_nlist_cell_build_noalloc: periodic image shift beyond +-127 cells");
+    return FACEK_EUNSUPPORTED;
+  }
+  return FACEK_OK;
+}
+
 }  // namespace
 }  // namespace facek
 
@@ -416,4 +509,14 @@ extern "C" int facek_nlist_reverse(const int32_t* row_ptr, const int32_t* ei, co
   if (E == 0) return FACEK_OK;
   reverse_k<<<ew_grid(E), 128, 0, as_stream(stream)>>>(row_ptr, ei, ej, S, E, rev);
   return launch_status("facek_nlist_reverse");
+}
+
+extern "C" int facek_nlist_cell_build_noalloc(int dtype, const double* pos, int64_t N, const double* cell, double rc,
+                                              int64_t max_edges, int32_t* row_ptr, int32_t* ei, int32_t* ej,
+                                              int32_t* S, void* shift, int64_t* n_edges, void* stream) {
+  FACEK_CHECK_ARG(N > 0 && rc > 0 && max_edges >= 0 && pos && cell && row_ptr && n_edges &&
+                      (max_edges == 0 || (ei && ej && S && shift)),
+                  "facek_nlist_cell_build_noalloc: bad arguments");
+  return FACEK_DISPATCH(dtype, build_noalloc, pos, N, cell, rc, max_edges, row_ptr, ei, ej, S, shift, n_edges,
+                        stream);
 }

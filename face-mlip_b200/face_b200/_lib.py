@@ -35,6 +35,7 @@ SIGNATURES = {
     "facek_nlist_batch_count": [P, I64, P, P, D, P, P],
     "facek_nlist_batch_fill": [I32, P, I64, P, P, D, P, P, P, P, P, P],
     "facek_nlist_reverse": [P, P, P, P, I64, I64, P, P],
+    "facek_nlist_cell_build_noalloc": [I32, P, I64, PD, D, I64, P, P, P, P, P, PI64, P],
     "facek_edge_vec": [I32, P, P, P, P, P, I64, P],
     "facek_edge_vec_bwd": [I32, P, P, P, I64, P, P],
     "facek_edge_sym": [I32, P, P, I64, P],

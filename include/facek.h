@@ -104,6 +104,19 @@ int facek_nlist_batch_fill(int dtype, const double* pos, int64_t N, const int32_
                            int32_t* S, void* shift, void* stream);
 int facek_nlist_reverse(const int32_t* row_ptr, const int32_t* ei, const int32_t* ej, const int32_t* S, int64_t N,
                         int64_t E, int32_t* rev, void* stream);
+/* Allocation-free periodic build (no counterpart in the reference): the same edge set, order and outputs as
+ * facek_nlist_cell_count + prefix sum + facek_nlist_cell_fill, for callers that cannot allocate device memory
+ * themselves (a host framework that hands out only preallocated buffers, or code running inside a memory pool
+ * or arena that forbids cudaMalloc).  The scratch lives in a file-scope device array of about 7.1 MB that every
+ * GPU loading the library holds until exit; limits: N <= 262,144 atoms and <= 65,536 cells.  The caller passes
+ * row_ptr (N+1) and output buffers of capacity max_edges; *n_edges receives the edge count (also when it exceeds
+ * max_edges, which returns FACEK_EINVAL with nothing filled, so the caller can retry with larger buffers).
+ * Calls no cudaMalloc/cudaFree.  The first call on a device looks up the scratch address (cudaGetSymbolAddress)
+ * and should come before any stream capture; the call synchronises the stream twice (edge count, error flag).
+ * All calls share the scratch array: calls that overlap on the GPU (other streams, other host threads) race. */
+int facek_nlist_cell_build_noalloc(int dtype, const double* pos, int64_t N, const double* cell, double rc,
+                                   int64_t max_edges, int32_t* row_ptr, int32_t* ei, int32_t* ej, int32_t* S,
+                                   void* shift, int64_t* n_edges, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------
  * Edge geometry: vec[e] = pos[ej] - pos[ei] + shift[e] (face/model.py:670) and its adjoint, the force gather
