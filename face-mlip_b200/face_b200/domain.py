@@ -1,0 +1,319 @@
+"""Multi-GPU evaluation: spatial decomposition of a periodic system, one process per GPU.
+
+The box (orthorhombic) is split into a grid of bricks (2x1x1, 2x2x1, 2x2x2, ...), one per rank.  A rank holds the
+atoms of its brick ("owned") plus every atom within `halo` = n_passes * rc of the brick along the split axes
+("ghosts", placed at the periodic image nearest the brick).  With that depth every owned atom's energy is computed
+exactly on the rank; ghosts only feed them.  Along unsplit axes the local system keeps the full periodicity, and the
+local extent along split axes stays below L - rc, so the local neighbour list is built with the original cell.
+
+Cross-rank coupling, all through differentiable collectives (torch.distributed.nn):
+  * latent-charge neutrality: mu = (Q + sum chi/J) / sum 1/J over all atoms -> two all-reduced sums
+    (face-mlip face/electrostatics.py:165-167);
+  * charges: the owned charges of all ranks are all-gathered into the global charge vector, which feeds the
+    real-space term of the owned rows and the PME reciprocal sum (computed redundantly on every rank on the full
+    mesh and counted once, 1/world per rank);
+  * forces: every rank differentiates its own energy (owned atoms + its share of the global terms) with respect to
+    the global positions; one all-reduce (sum) of that gradient gives the forces.
+Batches of non-periodic structures (molecules) are instead sharded by structure with no data-path collective.
+"""
+import json
+import math
+import os
+import statistics
+import sys
+import time
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+KE = 14.399645
+
+
+def brick_grid(world):
+    """Most cubic factorisation nx >= ny >= nz of the world size."""
+    best = None
+    for nx in range(1, world + 1):
+        if world % nx:
+            continue
+        for ny in range(1, world // nx + 1):
+            if (world // nx) % ny:
+                continue
+            nz = world // (nx * ny)
+            g = tuple(sorted((nx, ny, nz), reverse=True))
+            score = max(g) / min(g)
+            if best is None or score < best[0]:
+                best = (score, g)
+    return best[1]
+
+
+def select_local(pos, L, grid, rank, halo):
+    """Owned atoms and ghost images of brick `rank` (row-major over grid).  pos (N,3) float64 on any device, L (3,)
+    box lengths.  Returns gid (local -> global index, sorted), img (local image shift, so that local position =
+    pos[gid] + img), owned (bool)."""
+    dev = pos.device
+    Lt = torch.as_tensor(L, dtype=torch.float64, device=dev)
+    f = pos / Lt
+    fl = torch.floor(f)
+    fw = f - fl                                                   # wrapped fractional coordinates in [0, 1)
+    n = torch.as_tensor(grid, device=dev)
+    b = torch.clamp((fw * n).long(), max=n - 1)
+    rb = [(rank // (grid[1] * grid[2])) % grid[0], (rank // grid[2]) % grid[1], rank % grid[2]]
+    owned = (b[:, 0] == rb[0]) & (b[:, 1] == rb[1]) & (b[:, 2] == rb[2])
+    keep = torch.ones(pos.shape[0], dtype=torch.bool, device=dev)
+    img = torch.zeros_like(pos)
+    for d in range(3):
+        if grid[d] == 1:
+            continue
+        lo, hi = rb[d] / grid[d], (rb[d] + 1) / grid[d]
+        ks = torch.tensor([-1.0, 0.0, 1.0], dtype=torch.float64, device=dev)
+        x = fw[:, d, None] + ks[None]                             # candidate images
+        dd = torch.clamp(torch.maximum(lo - x, x - hi), min=0.0) * float(L[d])
+        best = dd.argmin(1)
+        keep &= dd.gather(1, best[:, None])[:, 0] <= halo
+        img[:, d] = (ks[best] - fl[:, d]) * float(L[d])           # wrapped position + k L - original position
+    local = keep | owned
+    gid = torch.nonzero(local)[:, 0]
+    return gid, img[gid], owned[gid]
+
+
+class LocalSystem:
+    """Positions-only view of a rank's local atoms (ASE-like for the neighbour builder)."""
+
+    def __init__(self, positions, numbers, cell):
+        self.positions = positions
+        self.numbers = numbers
+        self.cell = cell
+        self.pbc = True
+        self.charge = 0.0
+
+
+def rank_energy(pos_global, gid, img, owned, local_model, coulomb=None, world=1, group=None):
+    """This rank's share of the total energy as a differentiable function of the global positions.
+
+    local_model(pos_local) -> (e_at, h): per-atom model energies and final features of the local atoms.
+    coulomb (optional): dict with
+        head(h) -> (chi, J);  real_rows(pos_local, q_local) -> e_row;  pme(pos_global, q_global) -> scalar;
+        gp, volume, charge (total charge Q), n_global, gid_owned_all (global ids of every rank's owned atoms in
+        all-gather order, padded with -1), max_owned.
+    Sum over ranks = the system's energy."""
+    from torch.distributed.nn import functional as dnn
+    pos_local = pos_global[gid] + img
+    e_at, h = local_model(pos_local)
+    w = owned.to(e_at.dtype)
+    e = (e_at * w).sum()
+    if coulomb is None:
+        return e
+    chi, J = coulomb["head"](h)
+    oi = torch.nonzero(owned)[:, 0]
+    chi_o, J_o = chi[oi], J[oi]
+    allr = (lambda x: dnn.all_reduce(x, group=group)) if world > 1 else (lambda x: x)
+    s1 = allr((chi_o / J_o).sum())
+    s2 = allr((1.0 / J_o).sum())
+    mu = (coulomb["charge"] + s1) / s2
+    q_o = -(chi_o - mu) / J_o
+    # global charges: pad, all-gather, scatter by global id
+    n_g = coulomb["n_global"]
+    if world > 1:
+        pad = q_o.new_zeros(coulomb["max_owned"])
+        pad = torch.cat([q_o, pad[q_o.shape[0]:]])
+        parts = dnn.all_gather(pad, group=group)
+        flat = torch.cat(list(parts))
+    else:
+        flat = q_o
+    ids = coulomb["gid_owned_all"]
+    valid = ids >= 0
+    q_g = flat.new_zeros(n_g).index_put((ids[valid],), flat[valid])
+    q_loc = q_g[gid]
+    e_row = coulomb["real_rows"](pos_local, q_loc)
+    e_real = (e_row * w).sum()
+    e_recip = coulomb["pme"](pos_global, q_g)
+    gp = coulomb["gp"]
+    self_o = -(q_o * q_o).sum() / (math.sqrt(math.pi) * gp)
+    qsum = allr(q_o.sum())
+    bg = -0.5 * math.pi * gp ** 2 / coulomb["volume"] * qsum * qsum
+    e_es = KE * (e_real + e_recip / world + self_o + bg / world)
+    return e + (chi_o * q_o + 0.5 * J_o * q_o * q_o).sum() + e_es
+
+
+def owned_ids_all(gid, owned, world, group=None):
+    """Global ids of every rank's owned atoms in all-gather order, each rank padded to the largest count with -1."""
+    mine = gid[owned]
+    cnt = torch.tensor([mine.numel()], device=gid.device)
+    if world == 1:
+        return mine, int(mine.numel())
+    cnts = [torch.zeros_like(cnt) for _ in range(world)]
+    dist.all_gather(cnts, cnt, group=group)
+    mx = int(max(int(c) for c in cnts))
+    pad = torch.full((mx,), -1, dtype=mine.dtype, device=gid.device)
+    pad[:mine.numel()] = mine
+    parts = [torch.empty_like(pad) for _ in range(world)]
+    dist.all_gather(parts, pad, group=group)
+    return torch.cat(parts), mx
+
+
+# --------------------------------------------------------------------------------------------- GPU engine hooks
+class EngineParts:
+    """Callables of rank_energy backed by the CUDA engine (face_b200.ops)."""
+
+    def __init__(self, model, graph, pme_mesh, cell64):
+        from . import ops
+        self.ops = ops
+        self.model = model
+        self.g = graph
+        self.cell64 = cell64
+        self.P = None
+        self.geo = None
+        self.pme_mesh = pme_mesh
+
+    def local_model(self, pos_local):
+        e_at, h, P, gr, geo = self.ops.local_energies(self.model, self.g, pos_local)
+        self.P, self.gr, self.geo = P, gr, geo
+        return e_at, h
+
+    def head(self, h):
+        c = self.P["coulomb"]
+        import torch.nn.functional as F
+        chi, hard = self.ops._layer(c["h2"], F.silu(self.ops._layer(c["h0"], h))).unbind(-1)
+        return chi, F.softplus(hard) + 0.1
+
+    def real_rows(self, pos_local, q_local):
+        c = self.P["coulomb"]
+        return self.ops.CoulombReal.apply(self.geo["vec"], q_local.contiguous(), self.gr, c["gamma"], c["gp"])
+
+    def pme(self, pos_global, q_global):
+        c = self.P["coulomb"]
+        return self.ops.PMERecip.apply(pos_global, q_global.contiguous(), self.cell64, c["gp"], tuple(self.pme_mesh))
+
+
+class DistributedModel:
+    """Energy and forces of one periodic structure on `world` GPUs (this process = one rank)."""
+
+    def __init__(self, model, structure, rank, world, device, dtype=torch.float32, group=None):
+        from .neighbors import build_graph
+        self.model, self.rank, self.world, self.dev, self.dtype, self.group = model, rank, world, device, dtype, group
+        cell = np.asarray(structure.cell, np.float64)
+        if np.abs(cell - np.diag(np.diag(cell))).max() > 0:
+            raise NotImplementedError("spatial decomposition needs an orthorhombic cell")
+        self.L = np.diag(cell).copy()
+        self.cell64 = cell
+        self.grid = brick_grid(world)
+        self.halo = model.n_passes * model.rc
+        for d in range(3):
+            if self.grid[d] > 1 and self.L[d] / self.grid[d] + 2 * self.halo + model.rc >= self.L[d]:
+                raise ValueError(f"box too small for a {self.grid} decomposition with halo {self.halo} A")
+        self.numbers = np.asarray(structure.numbers, np.int64)
+        self.n_global = len(self.numbers)
+        self.Q = float(getattr(structure, "charge", 0.0))
+        self.build_graph = build_graph
+        self.setup(torch.as_tensor(np.asarray(structure.positions), dtype=torch.float64, device=device))
+
+    def setup(self, pos64):
+        """(Re)build the decomposition and the local neighbour list for global positions pos64 (device)."""
+        gid, img, owned = select_local(pos64, self.L, self.grid, self.rank, self.halo)
+        self.gid, self.img, self.owned = gid, img, owned
+        loc = LocalSystem((pos64[gid] + img).cpu().numpy(), self.numbers[gid.cpu().numpy()], self.cell64)
+        self.graph = self.build_graph([loc], self.model.rc, device=self.dev, dtype=self.dtype)
+        self.img_t = img.to(self.dtype)
+        tm = self.model.terms["coulomb"] if "coulomb" in self.model.terms else None
+        self.parts = EngineParts(self.model, self.graph, None, self.cell64)
+        self.coulomb = None
+        if tm is not None:
+            ids, mx = owned_ids_all(gid, owned, self.world, self.group)
+            mesh = tm.mesh or tuple(max(8, int(math.ceil(L / (tm.gp / 4.0)))) for L in self.L)
+            self.parts.pme_mesh = mesh
+            self.coulomb = {"head": self.parts.head, "real_rows": self.parts.real_rows, "pme": self.parts.pme,
+                            "gp": float(tm.gp), "volume": float(abs(np.linalg.det(self.cell64))), "charge": self.Q,
+                            "n_global": self.n_global, "gid_owned_all": ids, "max_owned": mx}
+
+    def energy_forces(self, pos_global):
+        """pos_global: (N,3) model-dtype device tensor of all atoms (same on every rank).  Returns (E_total, forces)
+        on every rank."""
+        pos = pos_global.detach().requires_grad_(True)
+        e = rank_energy(pos, self.gid, self.img_t, self.owned, self.parts.local_model, self.coulomb, self.world,
+                        self.group)
+        (g,) = torch.autograd.grad(e, pos)
+        g = g.contiguous()
+        et = e.detach().reshape(1).clone()
+        if self.world > 1:
+            dist.all_reduce(g, group=self.group)
+            dist.all_reduce(et, group=self.group)
+        return et[0], -g
+
+
+# --------------------------------------------------------------------------------------------- benchmark
+def bench_multi(a):
+    """bench.py --gpus N under torchrun: the 1,048,576-atom alloy decomposed over N GPUs (strong scaling)."""
+    import datetime
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+    import bench as B
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    try:
+        dtype = torch.float64 if a.config == 1 else torch.float32
+        structs, spec, pme = B.workload(a.config, scale=a.scale)
+        if a.scale and a.config == 5:
+            pme["mesh"] = tuple(max(8, int(round(n * a.scale / 64))) for n in pme["mesh"])
+        model = B.make_model(spec, pme, dev, dtype)
+        st = structs[0]
+        natoms = len(st.numbers)
+        dm = DistributedModel(model, st, rank, world, dev, dtype)
+        pos = torch.as_tensor(st.positions, dtype=dtype, device=dev)
+        n_local = int(dm.gid.numel())
+        for _ in range(a.warmup):
+            dm.energy_forces(pos)
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        with B.Clocks(local) as clk:
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0.record()
+            for _ in range(a.steps):
+                E, F = dm.energy_forces(pos)
+            e1.record()
+            torch.cuda.synchronize()
+            dist.barrier()
+        ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = float(ms)
+        # e2e: positions from pinned host memory, decomposition + local neighbour list rebuilt, forces to the host
+        e2e = None
+        if not a.no_e2e:
+            host = torch.as_tensor(st.positions, dtype=torch.float64).pin_memory()
+            ke = max(1, a.steps // 2)
+            torch.cuda.synchronize()
+            dist.barrier()
+            t0 = time.perf_counter()
+            for _ in range(ke):
+                p64 = host.to(dev, non_blocking=True)
+                dm.setup(p64)
+                E, F = dm.energy_forces(p64.to(dtype))
+                Fh = F.double().cpu()
+            torch.cuda.synchronize()
+            dist.barrier()
+            dt = torch.tensor([(time.perf_counter() - t0) / ke], device=dev)
+            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+            e2e = {"value": natoms / float(dt), "unit": B.UNIT, "h2d_bytes_per_step": natoms * 3 * 8,
+                   "d2h_bytes_per_step": natoms * 3 * 8, "ms_per_step": float(dt) * 1e3}
+        counts = torch.tensor([n_local], device=dev)
+        allc = [torch.zeros_like(counts) for _ in range(world)]
+        dist.all_gather(allc, counts)
+        if rank == 0:
+            out = {"metric": B.METRIC, "value": natoms * 1e3 / ms, "unit": B.UNIT, "n_gpus": world, "steps": a.steps,
+                   "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                   "vs_baseline": None, "dtype": "f32" if dtype == torch.float32 else "f64",
+                   "data": "synthetic (seeded geometry, seeded random-init weights)",
+                   "config": {"workload": f"cfg{a.config}: {natoms}-atom periodic system, spatial decomposition",
+                              "atoms": natoms, "bricks": list(dm.grid), "halo_A": dm.halo,
+                              "local_atoms_per_rank": [int(c) for c in allc],
+                              "l2": "inputs larger than L2", "parallelism": f"spatial {dm.grid} over NCCL"},
+                   "e2e": e2e, "energy": float(E), "clocks": clk.summary()}
+            print(json.dumps(out), flush=True)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()

@@ -525,6 +525,27 @@ def coulomb_term(P, gr, geo, h, pos):
     return chi * q + 0.5 * J * q * q + per_atom(e_es / natoms.to(q.dtype), batch, nstr), q
 
 
+def local_energies(model, gr, pos):
+    """Per-atom model energies (without physics terms) and final features h for positions `pos` (any
+    differentiable tensor) on graph `gr` (face/model.py:665-686)."""
+    dtype = model.embed.weight.dtype
+    P = prepare(model, dtype, pos.device)
+    P["max_body"] = model.max_body
+    zidx = P["zmap"][gr["Z"]]
+    gr = dict(gr, zidx=zidx.to(torch.int32).contiguous())
+    vec = EdgeVec.apply(pos, gr)
+    Y = EdgeSym.apply(vec)
+    geo = {"vec": vec, "Y": Y, "zidx": zidx, "avg_nb": P["avg_nb"]}
+    h = P["embed"][zidx]
+    e_at = P["E0"][zidx]
+    A_sets, eq = [], None
+    for t in range(len(P["blocks"])):
+        e, h, A, eq = block_forward(P, t, gr, geo, h, A_sets, eq)
+        A_sets.append(A)
+        e_at = e_at + P["scale"] * e
+    return e_at, h, P, gr, geo
+
+
 def face_forward(model, g, forces=True):
     """Energy (per structure), per-atom energy and forces for a graph dict (face/model.py:665-695).  `g` is either
     the engine's CSR graph (face_b200.neighbors.build_graph) or the reference's padded dict."""
@@ -532,26 +553,13 @@ def face_forward(model, g, forces=True):
     pos = g["pos"]
     if not pos.is_cuda:
         raise RuntimeError("face_b200 runs on CUDA only (no CPU path)")
-    dtype, dev = model.embed.weight.dtype, pos.device
-    P = prepare(model, dtype, dev)
-    P["max_body"] = model.max_body
+    dtype = model.embed.weight.dtype
     if pos.dtype != dtype:
         raise TypeError(f"positions are {pos.dtype}, model is {dtype}")
     if forces and not pos.requires_grad:
         pos.requires_grad_(True)
     with torch.set_grad_enabled(forces):
-        zidx = P["zmap"][gr["Z"]]
-        gr = dict(gr, zidx=zidx.to(torch.int32).contiguous())
-        vec = EdgeVec.apply(pos, gr)
-        Y = EdgeSym.apply(vec)
-        geo = {"vec": vec, "Y": Y, "zidx": zidx, "avg_nb": P["avg_nb"]}
-        h = P["embed"][zidx]
-        e_at = P["E0"][zidx]
-        A_sets, eq = [], None
-        for t in range(len(P["blocks"])):
-            e, h, A, eq = block_forward(P, t, gr, geo, h, A_sets, eq)
-            A_sets.append(A)
-            e_at = e_at + P["scale"] * e
+        e_at, h, P, gr, geo = local_energies(model, gr, pos)
         qv = None
         if "coulomb" in P:
             ea, qv = coulomb_term(P, gr, geo, h, pos)

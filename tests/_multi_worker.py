@@ -1,0 +1,50 @@
+"""Worker for tests/test_gpu_multi.py: fp64 alloy (cfg5 model, 15x15x15 cells, 54 A box) decomposed over the torchrun world;
+rank 0 compares energy and forces with the single-GPU engine and writes the differences to argv[1]."""
+import datetime
+import json
+import os
+import sys
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+sys.path.insert(0, ROOT)
+sys.path.insert(0, os.path.join(ROOT, "face-mlip_b200"))
+
+
+def main():
+    from face_b200 import systems
+    from face_b200.domain import DistributedModel
+    from face_b200.model import FACE
+    from face_b200.neighbors import build_graph
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    try:
+        spec = systems.model_kwargs(5)
+        kw = dict(spec)
+        mb = kw.pop("max_body")
+        m = FACE(**kw)
+        m.set_max_body(mb)
+        m.seed_(0)
+        m.set_pme(gp=1 / 0.32, mesh=(60, 60, 60))
+        m = m.to(dev, torch.float64)
+        st = systems.fcc(15, 3.6, 0.08, systems.MODELS[5]["elements"], seed=0)
+        dm = DistributedModel(m, st, rank, world, dev, torch.float64)
+        pos = torch.as_tensor(st.positions, dtype=torch.float64, device=dev)
+        E, F = dm.energy_forces(pos)
+        if rank == 0:
+            o = m(build_graph([st], 5.0, device=dev, dtype=torch.float64))
+            res = {"dE_rel": abs(float(E) - float(o["energy"][0])) / abs(float(o["energy"][0])),
+                   "dF": float((F - o["forces"]).abs().max()), "E": float(E)}
+            open(sys.argv[1], "w").write(json.dumps(res))
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,133 @@
+"""Spatial decomposition and its collective assembly (face_b200/domain.py) on two CPU ranks (gloo).
+
+The local model is the CPU oracle, so this checks the multi-GPU logic without a GPU: brick selection, ghost images,
+owned-atom energies, the all-reduced neutrality sums, the all-gathered global charges feeding real space and PME,
+and the all-reduced force gradient -- against the oracle evaluated on the whole periodic system in one process.
+"""
+import math
+import os
+import socket
+
+import numpy as np
+import pytest
+import torch
+import torch.distributed as dist
+import torch.multiprocessing as mp
+
+from oracle import face_ref, nlist
+
+SPEC = dict(elements=[24, 25, 26, 27, 28], C=8, n_basis=4, rc=4.0, n_passes=2, terms=("coulomb",), max_body=5,
+            radial_hidden=8, K_dir=4, norm="layer", transport=True, eqmsg=True, factor=True, B=4, K=4, cp=False,
+            unit=True)
+PME = {"gp": 1 / 0.32, "mesh": (24, 10, 10)}
+
+
+def _system():
+    from face_b200 import systems
+    st = systems.fcc(3, 3.6, 0.08, SPEC["elements"], seed=4)          # 3x3x3 cells; stretched along x below
+    reps = 4
+    pos = np.concatenate([st.positions + np.array([10.8 * r, 0, 0]) for r in range(reps)])
+    Z = np.tile(st.numbers, reps)
+    return systems.Structure(pos, Z, np.diag([10.8 * reps, 10.8, 10.8]), True, 0.0)
+
+
+def _state():
+    from face_b200.model import FACE
+    kw = dict(SPEC)
+    mb = kw.pop("max_body")
+    m = FACE(**kw)
+    m.set_max_body(mb)
+    return {k: v.double() if v.is_floating_point() else v for k, v in m.seed_(3).state_dict().items()}
+
+
+def _oracle_parts(P, cfg, g_local, cell):
+    gamma = 1.0
+    gp = PME["gp"]
+
+    def local_model(pos_local):
+        return face_ref.atom_energies(P, cfg, g_local, pos_local, torch.float64)
+
+    def head(h):
+        chi, hard = P.lin("terms.coulomb.head.2", torch.nn.functional.silu(P.lin("terms.coulomb.head.0", h))).unbind(-1)
+        return chi, torch.nn.functional.softplus(hard) + 0.1
+
+    nbr = torch.as_tensor(g_local["nbr"])
+    mask = torch.as_tensor(g_local["mask"])
+    shift = torch.as_tensor(g_local["shift"])
+
+    def real_rows(pos_local, q_local):
+        vec = pos_local[nbr] - pos_local[:, None] + shift
+        r = torch.sqrt(torch.where(mask, (vec * vec).sum(-1), torch.ones(mask.shape, dtype=torch.float64)))
+        K = torch.where(mask, (torch.erf(r / gamma) - torch.erf(r / gp)) / r, torch.zeros_like(r))
+        return 0.5 * q_local * (q_local[nbr] * K).sum(1)
+
+    def pme(pos_global, q_global):
+        return face_ref.pme_recip_energy(q_global, pos_global, torch.as_tensor(cell), gp, PME["mesh"])
+
+    return local_model, head, real_rows, pme
+
+
+def _worker(rank, world, port, out):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        from face_b200 import domain
+        st = _system()
+        cfg = dict(SPEC)
+        P = face_ref.Params(_state(), True, torch.float64)
+        pos_g = torch.as_tensor(st.positions, dtype=torch.float64)
+        L = np.diag(st.cell)
+        grid = domain.brick_grid(world)
+        gid, img, owned = domain.select_local(pos_g, L, grid, rank, cfg["n_passes"] * cfg["rc"])
+        loc = domain.LocalSystem((pos_g[gid] + img).numpy(), st.numbers[gid.numpy()], st.cell)
+        g_local = nlist.padded_graph([loc], cfg["rc"])
+        local_model, head, real_rows, pme = _oracle_parts(P, cfg, g_local, st.cell)
+        ids, mx = domain.owned_ids_all(gid, owned, world)
+        coul = {"head": head, "real_rows": real_rows, "pme": pme, "gp": PME["gp"],
+                "volume": float(abs(np.linalg.det(st.cell))), "charge": 0.0, "n_global": len(st.numbers),
+                "gid_owned_all": ids, "max_owned": mx}
+        pos = pos_g.clone().requires_grad_(True)
+        e = domain.rank_energy(pos, gid, img, owned, local_model, coul, world)
+        (g,) = torch.autograd.grad(e, pos)
+        et = e.detach().reshape(1).clone()
+        dist.all_reduce(g)
+        dist.all_reduce(et)
+        if rank == 0:
+            out.put((float(et[0]), (-g).numpy(), int(owned.sum()), int(gid.numel())))
+    finally:
+        dist.destroy_process_group()
+
+
+def _free_port():
+    s = socket.socket()
+    s.bind(("127.0.0.1", 0))
+    p = s.getsockname()[1]
+    s.close()
+    return p
+
+
+def test_two_rank_decomposition_matches_single_system():
+    st = _system()
+    cfg = dict(SPEC)
+    g = nlist.padded_graph([st], cfg["rc"])
+    ref = face_ref.forward(_state(), cfg, g, torch.float64, pme=PME)
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = _free_port()
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    E, F, n_owned, n_local = q.get(timeout=600)
+    for p in procs:
+        p.join(timeout=120)
+        assert p.exitcode == 0
+    assert n_local > n_owned                       # ghosts present
+    assert abs(E - float(ref["energy"][0])) <= 1e-10 * abs(float(ref["energy"][0]))
+    assert np.abs(F - ref["forces"].numpy()).max() <= 1e-9
+
+
+def test_brick_grid():
+    from face_b200.domain import brick_grid
+    assert brick_grid(1) == (1, 1, 1) and brick_grid(2) == (2, 1, 1)
+    assert brick_grid(4) == (2, 2, 1) and brick_grid(8) == (2, 2, 2)

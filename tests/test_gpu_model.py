@@ -125,3 +125,17 @@ def test_periodic_invariances_fp64():
     orr = run(r)
     assert abs(float(orr["energy"][0]) - E) < 1e-3 * (1 + abs(E))
     assert np.abs(orr["forces"].cpu().numpy() - F @ Q.T).max() < 1e-3
+
+
+def test_distributed_model_single_rank_matches_engine():
+    """The decomposition driver on one rank (one brick, no ghosts) reproduces the plain engine, Coulomb included."""
+    from face_b200 import systems
+    from face_b200.domain import DistributedModel
+    from face_b200.neighbors import build_graph
+    structs, spec, pme, d = case_inputs("cfg5_small")
+    m = _engine(spec, 0, pme, torch.float64)
+    dm = DistributedModel(m, structs[0], 0, 1, torch.device("cuda"), torch.float64)
+    pos = torch.as_tensor(structs[0].positions, dtype=torch.float64, device="cuda")
+    E, F = dm.energy_forces(pos)
+    assert abs(float(E) - d["energy64"][0]) <= 1e-10 * abs(d["energy64"][0])
+    assert np.abs(F.cpu().numpy() - d["forces64"]).max() <= 1e-9
