@@ -4,6 +4,8 @@
 #include <stdint.h>
 #include <cstdarg>
 #include <cstdio>
+#include <algorithm>
+#include <type_traits>
 
 #include "../../include/facek.h"
 
@@ -13,6 +15,12 @@ void set_error(const char* fmt, ...);
 int launch_status(const char* what);      // FACEK_OK or FACEK_ELAUNCH with the CUDA error recorded
 int sm_count();                           // multiprocessors of the current device (cached per device)
 int max_smem_optin();                     // opt-in shared memory per block (bytes)
+
+// tensor-core radial MLP (radial_tc.cu), fp32 only
+bool radial_tc_supported(int n_el, int nb, int H, int B);
+int radial_tc_fwd(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
+                  int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2,
+                  const void* b2, const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

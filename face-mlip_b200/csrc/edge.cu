@@ -4,16 +4,12 @@
 // All scatter-to-neighbour adjoints use the reverse-edge index of the symmetric neighbour list (gathers,
 // no atomics, deterministic).
 #include "common.cuh"
+#include "radial.cuh"
 
 namespace facek {
 namespace {
 
 constexpr int NX = 20;
-
-template <typename T>
-__device__ __forceinline__ T sigmoid(T z) {
-  return T(1) / (T(1) + exp(-z));
-}
 
 // ------------------------------------------------------------------------------------------ geometry
 template <typename T>
@@ -106,20 +102,6 @@ __global__ void edge_sym_bwd_k(const T* __restrict__ vec, const T* __restrict__ 
 }
 
 // ------------------------------------------------------------------------------------------ radial
-// polynomial envelope p = 6 (face/model.py:34-37) and its r-derivative
-template <typename T>
-__device__ __forceinline__ void envelope(T r, T rc, T& env, T& denv) {
-  const T x = r / rc;
-  if (x >= T(1)) {
-    env = 0;
-    denv = 0;
-    return;
-  }
-  const T x2 = x * x, x5 = x2 * x2 * x, x6 = x5 * x, x7 = x6 * x, x8 = x7 * x;
-  env = T(1) - T(28) * x6 + T(48) * x7 - T(21) * x8;
-  denv = (T(-168) * x5 + T(336) * x6 - T(168) * x7) / rc;
-}
-
 template <typename T, int NBMAX, int HMAX, int BMAX>
 __global__ void __launch_bounds__(128) radial_mlp_k(const T* __restrict__ vec, const int32_t* __restrict__ ei,
                                                     const int32_t* __restrict__ ej, const int32_t* __restrict__ zidx,
@@ -671,9 +653,9 @@ int radial_launch(const void* vec, const int32_t* ei, const int32_t* ej, const i
 }
 
 template <typename T>
-int radial_fwd(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
-               int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2, const void* b2,
-               const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream) {
+int radial_simt(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
+                int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2, const void* b2,
+                const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream) {
   if (E == 0) return FACEK_OK;
   FACEK_CHECK_ARG(H <= 64 && B <= 32 && nb <= 16, "facek_radial_fwd: H=%d B=%d nb=%d exceed 64/32/16", H, B, nb);
   if (nb <= 8 && B <= 16)
@@ -684,6 +666,16 @@ int radial_fwd(const void* vec, const int32_t* ei, const int32_t* ej, const int3
                                         dphidr, E, stream);
   return radial_launch<T, 16, 64, 32>(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
                                       dphidr, E, stream);
+}
+
+// fp32 with the flagship shapes runs on the tensor cores (radial_tc.cu); fp64 and other shapes on the CUDA cores
+template <typename T>
+int radial_fwd(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
+               int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2, const void* b2,
+               const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream) {
+  if (std::is_same<T, float>::value && radial_tc_supported(n_el, nb, H, B))
+    return radial_tc_fwd(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi, dphidr, E, stream);
+  return radial_simt<T>(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi, dphidr, E, stream);
 }
 
 template <typename T>
@@ -815,6 +807,17 @@ extern "C" int facek_radial_fwd(int dtype, const void* vec, const int32_t* ei, c
   FACEK_CHECK_ARG(E == 0 || (vec && ei && ej && zidx && w1 && b1 && pair && w2 && b2 && w3 && b3 && phi && dphidr),
                   "facek_radial_fwd: null tensor");
   return FACEK_DISPATCH(dtype, radial_fwd, vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
+                        dphidr, E, stream);
+}
+extern "C" int facek_radial_simt_fwd(int dtype, const void* vec, const int32_t* ei, const int32_t* ej,
+                                     const int32_t* zidx, int32_t n_el, double rc, int32_t nb, int32_t H, int32_t B,
+                                     const void* w1, const void* b1, const void* pair, const void* w2, const void* b2,
+                                     const void* w3, const void* b3, void* phi, void* dphidr, int64_t E,
+                                     void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && n_el > 0 && rc > 0 && nb > 0 && H > 0 && B > 0, "facek_radial_simt_fwd: bad sizes");
+  FACEK_CHECK_ARG(E == 0 || (vec && ei && ej && zidx && w1 && b1 && pair && w2 && b2 && w3 && b3 && phi && dphidr),
+                  "facek_radial_simt_fwd: null tensor");
+  return FACEK_DISPATCH(dtype, radial_simt, vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
                         dphidr, E, stream);
 }
 extern "C" int facek_radial_spline_fwd(int dtype, const void* vec, const int32_t* ei, const int32_t* ej,

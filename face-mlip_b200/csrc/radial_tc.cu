@@ -1,0 +1,328 @@
+// Radial basis x radial MLP per edge on the tcgen05 tensor cores, with forward-mode dphi/dr
+// (face-mlip face/model.py:460-470 FactorBlock radial path, :34-37 envelope, :23-31 Bessel basis).
+//
+//   x_n   = sqrt(2/rc) sin(f_n r)/r * env(r)                       n < nb, f_n = (n+1) pi / rc
+//   a1    = silu(W1 x + b1 + pair[z_i, z_j])                        H = 64 hidden units
+//   a2    = silu(W2 a1 + b2)
+//   phi   = (W3 a2 + b3) * env(r),  dphi/dr by pushing d/dr through the same three layers
+//
+// One CTA = two warpgroups; each warpgroup owns a 128-edge tile (one edge per thread = one TMEM lane) and runs
+//   layer 1 on the CUDA cores -> W2 x [a1 | da1] on the tensor core -> silu epilogue -> W3 x [a2 | da2] on the
+//   tensor core -> phi, dphi/dr epilogue,
+// so one warpgroup's CUDA-core work overlaps the other's MMAs. The MMAs run kind::tf32 with the 3-term split,
+// which keeps fp32 accuracy (tc.cuh). Weights are split once per CTA into shared memory; the CTA is persistent
+// over tiles. Tensor memory: 128 fp32 columns per warpgroup (value and tangent accumulators of W2, later reused
+// for W3).
+#include "common.cuh"
+#include "radial.cuh"
+#include "tc.cuh"
+
+namespace facek {
+namespace {
+
+using namespace tc;
+
+constexpr int kH = 64;                               // hidden width
+constexpr int kRows = 128;                           // edges per warpgroup tile = MMA M
+constexpr int kThreads = 256;                        // two warpgroups
+constexpr uint32_t kPlane = kRows * kH * 4;          // one fp32 operand plane (32 KB)
+constexpr uint32_t kTmemCols = 256;
+
+struct Layout {
+  uint32_t a, w2, w3, w1, b1, b2, b3, pair, mbar, slot, abort_, total;
+};
+
+__host__ __device__ inline Layout layout_for(int NB, int BO, int n_el) {
+  Layout L;
+  L.a = 0;                                            // [wg][hi|lo] operand planes
+  L.w2 = L.a + 4 * kPlane;                            // W2 hi, lo (64 x 64)
+  L.w3 = L.w2 + 2 * kH * kH * 4;                      // W3 hi, lo (BO x 64)
+  L.w1 = L.w3 + 2 * BO * kH * 4;                      // W1 (64 x NB), zero-padded basis
+  L.b1 = L.w1 + kH * NB * 4;
+  L.b2 = L.b1 + kH * 4;
+  L.b3 = L.b2 + kH * 4;
+  L.pair = L.b3 + BO * 4;                             // pair embedding (n_el^2 x 64)
+  L.mbar = L.pair + n_el * n_el * kH * 4;             // 2 x 8 B
+  L.slot = L.mbar + 16;
+  L.abort_ = L.slot + 16;                             // 2 x 4 B
+  L.total = L.abort_ + 16;
+  return L;
+}
+
+template <int NB, int BO>
+__global__ void __launch_bounds__(kThreads, 1)
+    radial_tc_k(const float* __restrict__ vec, const int32_t* __restrict__ ei, const int32_t* __restrict__ ej,
+                const int32_t* __restrict__ zidx, int n_el, float rc, int nb, const float* __restrict__ w1,
+                const float* __restrict__ b1, const float* __restrict__ pair, const float* __restrict__ w2,
+                const float* __restrict__ b2, const float* __restrict__ w3, const float* __restrict__ b3,
+                float* __restrict__ phi, float* __restrict__ dphidr, int64_t E) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  const Layout L = layout_for(NB, BO, n_el);
+  unsigned char* w2s = sm + L.w2;
+  unsigned char* w3s = sm + L.w3;
+  float* w1s = reinterpret_cast<float*>(sm + L.w1);
+  float* b1s = reinterpret_cast<float*>(sm + L.b1);
+  float* b2s = reinterpret_cast<float*>(sm + L.b2);
+  float* b3s = reinterpret_cast<float*>(sm + L.b3);
+  float* pairs = reinterpret_cast<float*>(sm + L.pair);
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + L.mbar);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(sm + L.slot);
+  int* abort_ = reinterpret_cast<int*>(sm + L.abort_);
+
+  const int tid = threadIdx.x, warp = tid >> 5, wg = tid >> 7, row = tid & (kRows - 1);
+
+  // ---- weights -> shared memory (W2, W3 as tf32 hi/lo planes in the K-major operand layout)
+  for (int q = tid; q < kH * kH; q += kThreads) {
+    const float w = w2[q], hi = to_tf32(w);
+    const uint32_t off = kmajor_off(q / kH, q % kH, kH);
+    *reinterpret_cast<float*>(w2s + off) = hi;
+    *reinterpret_cast<float*>(w2s + kH * kH * 4 + off) = to_tf32(w - hi);
+  }
+  for (int q = tid; q < BO * kH; q += kThreads) {
+    const float w = w3[q], hi = to_tf32(w);
+    const uint32_t off = kmajor_off(q / kH, q % kH, BO);
+    *reinterpret_cast<float*>(w3s + off) = hi;
+    *reinterpret_cast<float*>(w3s + BO * kH * 4 + off) = to_tf32(w - hi);
+  }
+  for (int q = tid; q < kH * NB; q += kThreads) {
+    const int h = q / NB, n = q % NB;
+    w1s[q] = n < nb ? w1[h * nb + n] : 0.f;
+  }
+  for (int q = tid; q < kH; q += kThreads) {
+    b1s[q] = b1[q];
+    b2s[q] = b2[q];
+  }
+  for (int q = tid; q < BO; q += kThreads) b3s[q] = b3[q];
+  for (int q = tid; q < n_el * n_el * kH; q += kThreads) pairs[q] = pair[q];
+  if (tid == 0) {
+    abort_[0] = 0;
+    abort_[1] = 0;
+    mbar_init(&mbar[0], 1);
+    mbar_init(&mbar[1], 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(slot, kTmemCols);
+    tmem_relinquish();
+  }
+  fence_proxy_async_smem();
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tbase = *slot;
+
+  unsigned char* a_hi = sm + L.a + wg * 2 * kPlane;
+  unsigned char* a_lo = a_hi + kPlane;
+  const uint32_t a_hi_s = smem_u32(a_hi), a_lo_s = a_hi_s + kPlane;
+  const uint32_t w2_hi_s = smem_u32(w2s), w2_lo_s = w2_hi_s + kH * kH * 4;
+  const uint32_t w3_hi_s = smem_u32(w3s), w3_lo_s = w3_hi_s + BO * kH * 4;
+  const uint32_t col0 = tbase + wg * 128;                                   // this warpgroup's columns
+  const uint32_t tl = col0 + ((uint32_t)((warp & 3) * 32) << 16);          // + this warp's lane quarter
+  volatile int* ab = &abort_[wg];
+  uint32_t parity = 0;
+
+  // one MMA round: operand writes -> async proxy, sync the warpgroup, one thread issues D = A . B^T over
+  // K = 64 in 8 steps x 3 split terms, commits, and everyone waits for completion
+  auto round = [&](uint32_t dcol, uint32_t b_hi, uint32_t b_lo, uint32_t b_rows, uint32_t idesc) {
+    fence_proxy_async_smem();
+    fence_before_sync();
+    bar_sync(1 + wg, kRows);
+    if (row == 0 && !*ab) {
+      fence_after_sync();
+#pragma unroll
+      for (int s = 0; s < kH / 8; s++) {
+        const uint64_t ah = desc_kmajor(a_hi_s + s * 2 * kRows * 16, kRows * 16, 128);
+        const uint64_t al = desc_kmajor(a_lo_s + s * 2 * kRows * 16, kRows * 16, 128);
+        const uint64_t bh = desc_kmajor(b_hi + s * 2 * b_rows * 16, b_rows * 16, 128);
+        const uint64_t bl = desc_kmajor(b_lo + s * 2 * b_rows * 16, b_rows * 16, 128);
+        mma_tf32(dcol, ah, bh, idesc, s > 0 ? 1u : 0u);
+        mma_tf32(dcol, ah, bl, idesc, 1u);
+        mma_tf32(dcol, al, bh, idesc, 1u);
+      }
+      commit(&mbar[wg]);
+    }
+    mbar_wait(&mbar[wg], parity, ab);
+    parity ^= 1u;
+    fence_after_sync();
+  };
+
+  const float cb = sqrtf(2.f / rc);
+  const float pi = 3.14159265358979323846f;
+  const int64_t ntiles = (E + kRows - 1) / kRows;
+  for (int64_t t = (int64_t)blockIdx.x * 2 + wg; t < ntiles; t += (int64_t)gridDim.x * 2) {
+    bar_sync(1 + wg, kRows);
+    if (*ab) break;                                  // uniform: nothing writes the flag between these points
+    const int64_t e = t * kRows + row;
+    const bool valid = e < E;
+    float r = 0.5f * rc;
+    int p = 0;
+    if (valid) {
+      const float vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+      r = sqrtf(vx * vx + vy * vy + vz * vz);
+      p = zidx[ei[e]] * n_el + zidx[ej[e]];
+    }
+    float env, denv;
+    envelope(r, rc, env, denv);
+    float rb[NB], drb[NB];
+#pragma unroll
+    for (int n = 0; n < NB; n++) {
+      rb[n] = 0.f;
+      drb[n] = 0.f;
+      if (n < nb) {
+        const float f = float(n + 1) * pi / rc;
+        const float s = sinf(f * r), co = cosf(f * r);
+        const float bes = s / r * cb;
+        const float dbes = (f * co / r - s / (r * r)) * cb;
+        rb[n] = bes * env;
+        drb[n] = dbes * env + bes * denv;
+      }
+    }
+    // ---- layer 1 on the CUDA cores: a1 -> operand planes, da1 kept in registers
+    const float* prow = pairs + p * kH;
+    float da1[kH];
+#pragma unroll
+    for (int h0 = 0; h0 < kH; h0 += 4) {
+      float a[4];
+#pragma unroll
+      for (int j = 0; j < 4; j++) {
+        const int h = h0 + j;
+        float z = b1s[h] + prow[h], dz = 0.f;
+#pragma unroll
+        for (int n = 0; n < NB; n++) {
+          z += w1s[h * NB + n] * rb[n];
+          dz += w1s[h * NB + n] * drb[n];
+        }
+        const float sg = sigmoid(z);
+        a[j] = z * sg;
+        da1[h] = sg * (1.f + z * (1.f - sg)) * dz;
+      }
+      store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), a[0], a[1], a[2], a[3]);
+    }
+    round(col0, w2_hi_s, w2_lo_s, kH, idesc_tf32(kRows, kH));                // z2 -> columns [0, 64)
+#pragma unroll
+    for (int h0 = 0; h0 < kH; h0 += 4)
+      store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), da1[h0], da1[h0 + 1], da1[h0 + 2], da1[h0 + 3]);
+    round(col0 + 64, w2_hi_s, w2_lo_s, kH, idesc_tf32(kRows, kH));           // dz2 -> columns [64, 128)
+
+    // ---- silu epilogue of layer 2: a2 -> operand planes, da2 kept in registers
+    float da2[kH];
+#pragma unroll
+    for (int c0 = 0; c0 < kH; c0 += 16) {
+      float z[16], dz[16];
+      tmem_ld16(tl + c0, z);
+      tmem_ld16(tl + 64 + c0, dz);
+      tmem_wait_ld();
+      float a[16];
+#pragma unroll
+      for (int j = 0; j < 16; j++) {
+        const float zz = z[j] + b2s[c0 + j];
+        const float sg = sigmoid(zz);
+        a[j] = zz * sg;
+        da2[c0 + j] = sg * (1.f + zz * (1.f - sg)) * dz[j];
+      }
+#pragma unroll
+      for (int q = 0; q < 16; q += 4)
+        store_split4(a_hi, a_lo, kmajor_off(row, c0 + q, kRows), a[q], a[q + 1], a[q + 2], a[q + 3]);
+    }
+    round(col0, w3_hi_s, w3_lo_s, BO, idesc_tf32(kRows, BO));                // z3 -> columns [0, BO)
+#pragma unroll
+    for (int h0 = 0; h0 < kH; h0 += 4)
+      store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), da2[h0], da2[h0 + 1], da2[h0 + 2], da2[h0 + 3]);
+    round(col0 + 32, w3_hi_s, w3_lo_s, BO, idesc_tf32(kRows, BO));           // dz3 -> columns [32, 32 + BO)
+
+    // ---- output epilogue
+#pragma unroll
+    for (int c0 = 0; c0 < BO; c0 += 16) {
+      float z[16], dz[16];
+      tmem_ld16(tl + c0, z);
+      tmem_ld16(tl + 32 + c0, dz);
+      tmem_wait_ld();
+      if (valid) {
+#pragma unroll
+        for (int q = 0; q < 16; q += 4) {
+          float v[4], d[4];
+#pragma unroll
+          for (int j = 0; j < 4; j++) {
+            v[j] = z[q + j] + b3s[c0 + q + j];
+            d[j] = dz[q + j] * env + v[j] * denv;
+            v[j] *= env;
+          }
+          *reinterpret_cast<float4*>(phi + e * BO + c0 + q) = make_float4(v[0], v[1], v[2], v[3]);
+          *reinterpret_cast<float4*>(dphidr + e * BO + c0 + q) = make_float4(d[0], d[1], d[2], d[3]);
+        }
+      }
+    }
+    fence_before_sync();
+  }
+  fence_before_sync();
+  __syncthreads();
+  if (warp == 0) {
+    fence_after_sync();
+    tmem_dealloc(tbase, kTmemCols);
+  }
+}
+
+template <int NB, int BO>
+int radial_tc_launch(const float* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, float rc,
+                     int nb, const float* w1, const float* b1, const float* pair, const float* w2, const float* b2,
+                     const float* w3, const float* b3, float* phi, float* dphidr, int64_t E, void* stream) {
+  const Layout L = layout_for(NB, BO, n_el);
+  FACEK_CHECK_ARG((int)L.total <= max_smem_optin(), "facek_radial_tc_fwd: %u B of shared memory needed", L.total);
+  cudaFuncSetAttribute(radial_tc_k<NB, BO>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)L.total);
+  const int64_t ntiles = (E + kRows - 1) / kRows;
+  const int grid = (int)std::min<int64_t>((ntiles + 1) / 2, sm_count());
+  radial_tc_k<NB, BO><<<grid, kThreads, L.total, as_stream(stream)>>>(vec, ei, ej, zidx, n_el, rc, nb, w1, b1, pair,
+                                                                       w2, b2, w3, b3, phi, dphidr, E);
+  return launch_status("facek_radial_tc_fwd");
+}
+
+}  // namespace
+
+bool radial_tc_supported(int n_el, int nb, int H, int B) {
+  if (H != kH || !(B == 16 || B == 32) || nb < 1 || nb > 16 || n_el < 1) return false;
+  return (int)layout_for(nb <= 8 ? 8 : 16, B, n_el).total <= max_smem_optin();
+}
+
+int radial_tc_fwd(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
+                  int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2,
+                  const void* b2, const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream) {
+  FACEK_CHECK_ARG(radial_tc_supported(n_el, nb, H, B),
+                  "facek_radial_tc_fwd: needs H = 64, B in {16, 32}, nb <= 16 (got H=%d B=%d nb=%d n_el=%d)", H, B,
+                  nb, n_el);
+  if (E == 0) return FACEK_OK;
+  auto f = [&](auto launch) {
+    return launch((const float*)vec, ei, ej, zidx, n_el, (float)rc, nb, (const float*)w1, (const float*)b1,
+                  (const float*)pair, (const float*)w2, (const float*)b2, (const float*)w3, (const float*)b3,
+                  (float*)phi, (float*)dphidr, E, stream);
+  };
+  if (nb <= 8) return B == 16 ? f(radial_tc_launch<8, 16>) : f(radial_tc_launch<8, 32>);
+  return B == 16 ? f(radial_tc_launch<16, 16>) : f(radial_tc_launch<16, 32>);
+}
+
+}  // namespace facek
+
+using namespace facek;
+
+extern "C" int facek_radial_tc_fwd(const float* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx,
+                                   int32_t n_el, double rc, int32_t nb, int32_t H, int32_t B, const float* w1,
+                                   const float* b1, const float* pair, const float* w2, const float* b2,
+                                   const float* w3, const float* b3, float* phi, float* dphidr, int64_t E,
+                                   void* stream) {
+  FACEK_CHECK_ARG(E >= 0 && n_el > 0 && rc > 0, "facek_radial_tc_fwd: bad sizes");
+  FACEK_CHECK_ARG(E == 0 || (vec && ei && ej && zidx && w1 && b1 && pair && w2 && b2 && w3 && b3 && phi && dphidr),
+                  "facek_radial_tc_fwd: null tensor");
+  return radial_tc_fwd(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi, dphidr, E, stream);
+}
+
+extern "C" int facek_tc_status(int32_t* status, int32_t clear) {
+  FACEK_CHECK_ARG(status != nullptr, "facek_tc_status: null output");
+  int v = 0;
+  if (cudaMemcpyFromSymbol(&v, tc::g_tc_status, sizeof(int)) != cudaSuccess) return launch_status("facek_tc_status");
+  if (clear && v) {
+    const int zero = 0;
+    if (cudaMemcpyToSymbol(tc::g_tc_status, &zero, sizeof(int)) != cudaSuccess)
+      return launch_status("facek_tc_status");
+  }
+  *status = v;
+  return FACEK_OK;
+}

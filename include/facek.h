@@ -142,6 +142,22 @@ int facek_radial_fwd(int dtype, const void* vec, const int32_t* ei, const int32_
                      int32_t n_el, double rc, int32_t nb, int32_t H, int32_t B, const void* w1, const void* b1,
                      const void* pair, const void* w2, const void* b2, const void* w3, const void* b3, void* phi,
                      void* dphidr, int64_t E, void* stream);
+/* facek_radial_fwd runs fp32 with H = 64, B in {16, 32}, nb <= 16 on the tcgen05 tensor cores (fp32 accuracy through
+ * the 3-term tf32 split); fp64 and other shapes on the CUDA cores. The two explicit variants below pick one path;
+ * they have no reference counterpart (the reference has a single PyTorch path, face/model.py:465-469) and exist so
+ * that callers and tests can compare the paths. facek_radial_tc_fwd is fp32 only and returns FACEK_EINVAL for
+ * shapes it does not cover. */
+int facek_radial_simt_fwd(int dtype, const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx,
+                          int32_t n_el, double rc, int32_t nb, int32_t H, int32_t B, const void* w1, const void* b1,
+                          const void* pair, const void* w2, const void* b2, const void* w3, const void* b3, void* phi,
+                          void* dphidr, int64_t E, void* stream);
+int facek_radial_tc_fwd(const float* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int32_t n_el,
+                        double rc, int32_t nb, int32_t H, int32_t B, const float* w1, const float* b1,
+                        const float* pair, const float* w2, const float* b2, const float* w3, const float* b3,
+                        float* phi, float* dphidr, int64_t E, void* stream);
+/* Status of the tensor-core kernels (no reference counterpart): bit 0 set when a kernel gave up waiting for its
+ * MMAs (bounded wait) and returned early with its outputs incomplete. Synchronises the device; clear != 0 resets. */
+int facek_tc_status(int32_t* status, int32_t clear);
 int facek_radial_spline_fwd(int dtype, const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx,
                             int32_t n_el, double rc, int32_t G, double dr, int32_t B, const void* T, const void* dT,
                             void* phi, void* dphidr, int64_t E, void* stream);
