@@ -21,6 +21,8 @@ bool radial_tc_supported(int n_el, int nb, int H, int B);
 int radial_tc_fwd(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
                   int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2,
                   const void* b2, const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream);
+// bounded-wait status word of the tensor-core GEMM unit (gemm_tc.cu); -1 when it cannot be read
+int gemm_tc_status(int clear);
 
 inline cudaStream_t as_stream(void* s) { return reinterpret_cast<cudaStream_t>(s); }
 

@@ -7,7 +7,9 @@
 // contiguous, bank-conflict-free 512-byte store for each 4-float chunk.
 //
 // fp32 accuracy on the tf32 datapath uses the three-term split x = hi + lo (hi = tf32(x), lo = tf32(x - hi)):
-// A.B ~= Ahi.Bhi + Ahi.Blo + Alo.Bhi, dropping only the Alo.Blo term (relative size 2^-22).
+// A.B ~= Ahi.Bhi + Ahi.Blo + Alo.Bhi, dropping only the Alo.Blo term (relative size 2^-22). Where an operand is
+// fed to the tensor core as raw fp32, hi is the truncation the hardware applies and lo = tf32(x - trunc(x))
+// (dropped term 2^-21).
 //
 // Every wait here is bounded: a wait that runs out sets a status bit in g_tc_status (read and cleared through
 // facek_tc_status) and returns false; callers then skip the remaining work and release their tensor memory.
@@ -142,12 +144,15 @@ __device__ __forceinline__ void tmem_ld16(uint32_t taddr, float* v) {
 }
 __device__ __forceinline__ void tmem_wait_ld() { asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory"); }
 
-// round to tf32 (nearest, ties away), kept in an fp32 register with the low 13 mantissa bits zero
+// round to tf32 (nearest, ties away from zero), kept in an fp32 register with the low 13 mantissa bits zero.
+// Integer form: adding half of the dropped range to the magnitude bits and masking rounds the magnitude
+// half-up, the same result as cvt.rna.tf32.f32 for finite values, on the integer ALU instead of the
+// conversion pipe.
 __device__ __forceinline__ float to_tf32(float x) {
-  uint32_t r;
-  asm("cvt.rna.tf32.f32 %0, %1;" : "=r"(r) : "f"(x));
-  return __uint_as_float(r);
+  return __uint_as_float((__float_as_uint(x) + 0x1000u) & 0xFFFFE000u);
 }
+// the tf32 value the tensor core reads from an fp32 bit pattern (the low 13 mantissa bits ignored)
+__device__ __forceinline__ float tf32_trunc(float x) { return __uint_as_float(__float_as_uint(x) & 0xFFFFE000u); }
 
 // store 4 consecutive-k values of one row as (hi, lo) into two operand planes
 __device__ __forceinline__ void store_split4(unsigned char* hi_plane, unsigned char* lo_plane, uint32_t off,

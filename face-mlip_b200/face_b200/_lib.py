@@ -44,6 +44,9 @@ SIGNATURES = {
     "facek_radial_simt_fwd": [I32, P, P, P, P, I32, D, I32, I32, I32, P, P, P, P, P, P, P, P, P, I64, P],
     "facek_radial_tc_fwd": [P, P, P, P, I32, D, I32, I32, I32, P, P, P, P, P, P, P, P, P, I64, P],
     "facek_tc_status": [P, I32],
+    "facek_gemm_image_floats": [I64, I64],
+    "facek_gemm_pack": [P, I64, I64, I64, I64, P, P],
+    "facek_gemm_tc": [P, I64, I64, I64, P, I64, P, P, I64, I32, P],
     "facek_radial_spline_fwd": [I32, P, P, P, P, I32, D, I32, D, I32, P, P, P, P, I64, P],
     "facek_radial_bwd": [I32, P, P, P, I32, P, I32, I64, P],
     "facek_edge_msg_fwd": [I32, P, P, P, P, P, I32, I32, P, I64, I64, P],
@@ -60,6 +63,7 @@ SIGNATURES = {
 _lib = None
 
 # kernels launched per entry point (for launch accounting in the benchmark)
+RESTYPES = {"facek_gemm_image_floats": ctypes.c_int64}     # everything else returns an int status
 LAUNCHES_PER_CALL = {"facek_nlist_cell_count": 5, "facek_edge_msg_bwd": 2, "facek_transport_bwd": 2}
 CALLS = {}            # name -> number of calls since reset (only while COUNTING)
 COUNTING = False
@@ -79,7 +83,7 @@ def lib():
         for name, args in SIGNATURES.items():
             fn = getattr(L, name)
             fn.argtypes = args
-            fn.restype = ctypes.c_int
+            fn.restype = RESTYPES.get(name, ctypes.c_int)
         L.facek_last_error.restype = ctypes.c_char_p
         L.facek_last_error.argtypes = []
         L.facek_version.restype = ctypes.c_int

@@ -1,8 +1,9 @@
 """FACE energy+force engine on libfacek.so.
 
 Each edge- and node-level hot op is a torch.autograd.Function over one C-ABI kernel pair (forward + analytic
-backward); torch autograd only sequences them and sums their gradient contributions, and cuBLAS runs the
-channel-mixing GEMMs.  The forward follows face-mlip's FACE.forward / FactorBlock pass by pass
+backward); torch autograd only sequences them and sums their gradient contributions. In fp32 the channel-mixing
+GEMMs run on the library's tcgen05 GEMM with weights packed once per model (Dense); fp64 uses torch matmul.
+The forward follows face-mlip's FACE.forward / FactorBlock pass by pass
 (face/model.py:665-695, :310-339, :460-534, :204-308); the layouts differ where that removes copies:
 
 Every multi-component per-atom tensor is stored component-major, (components, N, channels), so each rank block
@@ -320,6 +321,85 @@ class PMERecip(torch.autograd.Function):
         return dpos, dq, None, None, None
 
 
+# ============================================================================================ channel GEMMs
+class Dense:
+    """A constant (K, N) fp32 weight packed for the tensor-core GEMM (facek_gemm_tc): the split image of W for
+    y = x @ W (+ b) and of W^T for the adjoint dx = dy @ W^T.  K and N must be multiples of 4."""
+
+    def __init__(self, W, b=None):
+        assert W.dtype == torch.float32 and W.is_cuda and W.dim() == 2
+        self.K, self.N = W.shape
+        self.b = None if b is None else b.contiguous()
+        self.img = self._pack(W, self.K, self.N, W.stride(0), W.stride(1))
+        self.imgT = self._pack(W, self.N, self.K, W.stride(1), W.stride(0))
+
+    @staticmethod
+    def _pack(W, K, N, sk, sn):
+        n = _lib.lib().facek_gemm_image_floats(K, N)
+        img = torch.empty(n, dtype=torch.float32, device=W.device)
+        _lib.call("facek_gemm_pack", _p(W), K, N, sk, sn, _p(img), _lib.stream())
+        return img
+
+    @staticmethod
+    def ok(K, N):
+        return K % 4 == 0 and N % 4 == 0
+
+
+def _gemm(x2, img, K, N, bias, out, beta):
+    _lib.call("facek_gemm_tc", _p(x2), x2.shape[0], K, x2.stride(0), _p(img), N, _p(bias), _p(out), out.stride(0),
+              beta, _lib.stream())
+
+
+def _rows(x, K):
+    """x as (rows, K) with unit column stride and 16-byte aligned rows (a copy only when the view is not)."""
+    x2 = x.reshape(-1, K)
+    return x2 if (x2.stride(1) == 1 and x2.stride(0) % 4 == 0 and x2.data_ptr() % 16 == 0) else x2.contiguous()
+
+
+class TCMatmul(torch.autograd.Function):
+    """y = x1 @ W1 (+ x2 @ W2) (+ b1) on the tensor cores; inputs (..., K_i), output (..., N); weights constant."""
+
+    @staticmethod
+    def forward(ctx, x1, d1, x2, d2):
+        lead = x1.shape[:-1]
+        a1 = _rows(x1, d1.K)
+        y = torch.empty(a1.shape[0], d1.N, dtype=x1.dtype, device=x1.device)
+        _gemm(a1, d1.img, d1.K, d1.N, d1.b, y, 0)
+        if x2 is not None:
+            _gemm(_rows(x2, d2.K), d2.img, d2.K, d2.N, d2.b, y, 1)
+        ctx.d1, ctx.d2, ctx.lead = d1, d2, lead
+        ctx.has2 = x2 is not None
+        return y.view(*lead, d1.N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        d1, d2 = ctx.d1, ctx.d2
+        g = _rows(dy, d1.N)
+        dx1 = torch.empty(g.shape[0], d1.K, dtype=dy.dtype, device=dy.device)
+        _gemm(g, d1.imgT, d1.N, d1.K, None, dx1, 0)
+        dx2 = None
+        if ctx.has2:
+            dx2 = torch.empty(g.shape[0], d2.K, dtype=dy.dtype, device=dy.device)
+            _gemm(g, d2.imgT, d2.N, d2.K, None, dx2, 0)
+            dx2 = dx2.view(*ctx.lead, d2.K)
+        return dx1.view(*ctx.lead, d1.K), None, dx2, None
+
+
+def mm(x, W, D=None, x2=None, W2=None, D2=None):
+    """x @ W (+ x2 @ W2): the tensor-core GEMM when packed weights D are given (fp32), else torch."""
+    if D is not None and x.dtype == torch.float32 and (x2 is None or D2 is not None):
+        return TCMatmul.apply(x, D, x2, D2)
+    y = x @ W
+    return y if x2 is None else y + x2 @ W2
+
+
+def linear(x, W, D=None):
+    """F.linear with (weight, bias) W, through the packed GEMM when available."""
+    if D is not None and x.dtype == torch.float32:
+        return TCMatmul.apply(x, D, None, None)
+    return F.linear(x, W[0], W[1])
+
+
 # ============================================================================================ weights
 def _lin(model, mod, dtype, dev):
     w = mod.weight.detach()
@@ -358,6 +438,10 @@ def prepare(model, dtype, dev):
         q["msg_w"], q["msg_b"] = _lin(model, blk.msg, dtype, dev)
         q["mixT"] = [(_lin(model, blk.mix[l], dtype, dev)[0]).t().contiguous() for l in range(4)]      # (BK, C)
         q["projT"] = [(_lin(model, blk.proj[l], dtype, dev)[0]).t().contiguous() for l in range(4)]    # (cin, 3C)
+        tc = dtype == torch.float32 and torch.device(dev).type == "cuda"
+        pk = (lambda W, b=None: Dense(W, b) if tc and Dense.ok(*W.shape) else None)
+        q["mixD"] = [pk(W) for W in q["mixT"]]
+        q["projD"] = [pk(W) for W in q["projT"]]
         q["elem_scale"] = d(blk.elem_scale.weight)
         q["norm"] = blk.norm_kind
         if blk.norm_kind == "layer":
@@ -365,9 +449,11 @@ def prepare(model, dtype, dev):
         elif blk.norm_kind == "affine":
             q["ln_w"], q["ln_b"] = d(blk.norm.w), d(blk.norm.b)
         q["out"] = [_lin(model, blk.out[i], dtype, dev) for i in (0, 2, 4)]
+        q["outD"] = [pk(w.t(), b) for w, b in q["out"]]
         if blk.eq_out:
             q["vpath"], q["mpath"] = d(blk.vpath), d(blk.mpath)
             q["gate"] = _lin(model, blk.gate, dtype, dev)
+            q["gateD"] = pk(q["gate"][0].t(), q["gate"][1])
         if blk.directional:
             wd, bd = _lin(model, blk.dir_mix, dtype, dev)                                 # (K, 4Kd)
             q["dir"] = [wd[:, i * Kd:(i + 1) * Kd].t().contiguous() for i in range(4)]       # each (Kd, K)
@@ -379,6 +465,7 @@ def prepare(model, dtype, dev):
             for name in ("tmix1", "tmix2"):
                 w = _lin(model, getattr(blk, name), dtype, dev)[0]                           # (C, B*2*Kd) cols (b,t,kd)
                 q[name + "T"] = w.view(C, B, 2, Kd).permute(0, 2, 1, 3).reshape(C, 2 * B * Kd).t().contiguous()
+                q[name + "D"] = pk(q[name + "T"])
         blocks.append(q)
     P["blocks"] = blocks
     if "coulomb" in model.terms:
@@ -443,15 +530,15 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
         mj = EdgeMsg.apply(Y, msgtab[None], None, gr)
     D = Density.apply(phi, mj, Y, gr)                                                # 4 x (k_l, N, B*K)
     s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1)   # (4, N, C)
-    A = [D[l] @ q["mixT"][l] for l in range(4)]                                      # (k_l, N, C)
+    tpl = {}
     if Gt is not None:
         T1, T2 = Transport.apply(phi, vec, Gt, gr)                                   # (3|6, N, 2*B*Kd)
-        A[1] = A[1] + T1 @ q["tmix1T"]
-        A[2] = A[2] + T2 @ q["tmix2T"]
+        tpl = {1: (T1, q["tmix1T"], q["tmix1D"]), 2: (T2, q["tmix2T"], q["tmix2D"])}
+    A = [mm(D[l], q["mixT"][l], q["mixD"][l], *tpl.get(l, (None, None, None))) for l in range(4)]   # (k_l, N, C)
     A = [A[l] * s[l] for l in range(4)]
     # invariants (face/model.py:204-270): projections straight into the node kernel's layout
     sets = A_sets + [A]
-    ys = [torch.cat([a[l] for a in sets], 2) @ q["projT"][l] for l in range(4)]     # (k_l, N, 3C)
+    ys = [mm(torch.cat([a[l] for a in sets], 2), q["projT"][l], q["projD"][l]) for l in range(4)]   # (k_l, N, 3C)
     a_w = q["vpath"] if q["eq_out"] else None
     b_w = q["mpath"] if q["eq_out"] else None
     inv, V, Ms = NodeAlgebraEngine.apply(*ys, a_w, b_w, q["eq_out"], P["max_body"])
@@ -460,10 +547,11 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
     elif q["norm"] == "affine":
         inv = inv * q["ln_w"] + q["ln_b"]
     z = torch.cat([inv, h, inv.new_zeros(N, 4)], 1)
-    o = _layer(q["out"][2], F.silu(_layer(q["out"][1], F.silu(_layer(q["out"][0], z)))))
+    o = linear(F.silu(linear(F.silu(linear(z, q["out"][0], q["outD"][0])), q["out"][1], q["outD"][1])),
+               q["out"][2], q["outD"][2])
     eq_new = None
     if q["eq_out"]:
-        gv, gm = _layer(q["gate"], inv).chunk(2, dim=-1)
+        gv, gm = linear(inv, q["gate"], q["gateD"]).chunk(2, dim=-1)
         eq_new = (V * gv[None], Ms * gm[None])
     return o[:, 0], h + o[:, 1:], A, eq_new
 

@@ -155,6 +155,19 @@ int facek_radial_tc_fwd(const float* vec, const int32_t* ei, const int32_t* ej, 
                         double rc, int32_t nb, int32_t H, int32_t B, const float* w1, const float* b1,
                         const float* pair, const float* w2, const float* b2, const float* w3, const float* b3,
                         float* phi, float* dphidr, int64_t E, void* stream);
+/* Dense fp32 GEMM on the tcgen05 tensor cores for the channel maps (face/model.py:502-534 mix / tmix / proj,
+ * :324-339 output MLP and gate; the reference calls torch.nn.Linear there):
+ *   C[M, N] (beta ? += : =) A[M, K] . W[K, N] (+ bias[N]),  fp32 accuracy through the 3-term tf32 split, each
+ *   32-wide K chunk accumulated separately and the chunk partials summed in fp32 with round-to-nearest.
+ * W is packed once into an image of facek_gemm_image_floats(K, N) floats by facek_gemm_pack (W[k, n] at
+ * W[k*stride_k + n*stride_n], so a transposed view packs W^T for the adjoint). A, C row-major with leading
+ * dimensions lda, ldc; K, N, lda, ldc multiples of 4 and A, C, image 16-byte aligned (FACEK_EINVAL otherwise).
+ * No reference counterpart as a C entry point. */
+int64_t facek_gemm_image_floats(int64_t K, int64_t N);
+int facek_gemm_pack(const float* W, int64_t K, int64_t N, int64_t stride_k, int64_t stride_n, float* image,
+                    void* stream);
+int facek_gemm_tc(const float* A, int64_t M, int64_t K, int64_t lda, const float* image, int64_t N,
+                  const float* bias, float* C, int64_t ldc, int32_t beta, void* stream);
 /* Status of the tensor-core kernels (no reference counterpart): bit 0 set when a kernel gave up waiting for its
  * MMAs (bounded wait) and returned early with its outputs incomplete. Synchronises the device; clear != 0 resets. */
 int facek_tc_status(int32_t* status, int32_t clear);

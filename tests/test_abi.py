@@ -14,7 +14,7 @@ def _declared():
     src = open(HEADER).read()
     src = re.sub(r"/\*.*?\*/", "", src, flags=re.S)
     out = {}
-    for m in re.finditer(r"(?:int|const char\*)\s+(facek_\w+)\s*\(([^)]*)\)\s*;", src):
+    for m in re.finditer(r"(?:int64_t|int|const char\*)\s+(facek_\w+)\s*\(([^)]*)\)\s*;", src):
         params = [p for p in m.group(2).split(",") if p.strip() and p.strip() != "void"]
         out[m.group(1)] = len(params)
     return out

@@ -1,0 +1,90 @@
+"""Tensor-core GEMM (facek_gemm_tc, tcgen05 kind::tf32 with the 3-term split and per-chunk fp32 partial sums)
+against float64 torch on the same inputs: ragged M, K and N tails, strided A, bias and accumulate epilogues, the
+wide-N tiling, and the autograd Function the engine routes its channel maps through (face-mlip
+face/model.py:502-534, :324-339 use torch.nn.Linear there).  Bar: within 4x the error of torch's own fp32
+(CUDA-core) GEMM on the same inputs, or 2e-6 of the largest output."""
+import pytest
+import torch
+
+pytestmark = pytest.mark.gpu
+if not torch.cuda.is_available():
+    pytest.skip("needs a CUDA device", allow_module_level=True)
+
+DEV = "cuda"
+
+
+def _rel(a, b):
+    return float((a.double() - b).abs().max() / b.abs().max().clamp_min(1e-30))
+
+
+def _status():
+    import ctypes
+    from face_b200 import _lib
+    v = ctypes.c_int32(-1)
+    _lib.call("facek_tc_status", ctypes.byref(v), 1)
+    return v.value
+
+
+@pytest.mark.parametrize("M,K,N", [(1, 4, 4), (127, 32, 64), (128, 64, 192), (1000, 644, 128), (5000, 512, 64),
+                                   (3000, 64, 512), (300, 128, 192), (257, 36, 20), (70_001, 512, 64),
+                                   (2048, 576, 128), (129, 8, 256)])
+def test_gemm_matches_fp64(M, K, N):
+    from face_b200.ops import Dense, _gemm
+    g = torch.Generator(device=DEV).manual_seed(M + K + N)
+    A = torch.randn(M, K, device=DEV, generator=g)
+    W = torch.randn(K, N, device=DEV, generator=g) * K ** -0.5
+    b = torch.randn(N, device=DEV, generator=g)
+    d = Dense(W, b)
+    C = torch.full((M, N), float("nan"), device=DEV)
+    _gemm(A, d.img, K, N, d.b, C, 0)
+    ref = A.double() @ W.double() + b.double()
+    e_tc, e_32 = _rel(C, ref), _rel(A @ W + b, ref)
+    assert torch.isfinite(C).all()
+    assert e_tc < max(4 * e_32, 2e-6), (e_tc, e_32)
+    # adjoint image: dA = dC . W^T
+    G = torch.randn(M, N, device=DEV, generator=g)
+    dA = torch.empty(M, K, device=DEV)
+    _gemm(G, d.imgT, N, K, None, dA, 0)
+    r2 = G.double() @ W.double().t()
+    assert _rel(dA, r2) < max(4 * _rel(G @ W.t(), r2), 2e-6)
+    assert _status() == 0
+
+
+def test_gemm_strided_a_and_accumulate():
+    from face_b200.ops import Dense, _gemm
+    g = torch.Generator(device=DEV).manual_seed(1)
+    big = torch.randn(6000, 48, device=DEV, generator=g)
+    A = big[:, :32]                                                # lda = 48 > K = 32
+    W = torch.randn(32, 96, device=DEV, generator=g) / 6
+    C0 = torch.randn(6000, 96, device=DEV, generator=g)
+    C = C0.clone()
+    d = Dense(W)
+    _gemm(A, d.img, 32, 96, None, C, 1)
+    ref = C0.double() + A.double() @ W.double()
+    assert _rel(C, ref) < 2e-6
+    assert _status() == 0
+
+
+def test_gemm_rejects_unaligned_k():
+    from face_b200.ops import Dense, _gemm
+    d = Dense(torch.randn(8, 8, device=DEV))
+    A = torch.randn(10, 6, device=DEV)                             # K = 6 is not a multiple of 4
+    with pytest.raises(RuntimeError, match="facek_gemm_tc"):
+        _gemm(A, d.img, 6, 8, None, torch.empty(10, 8, device=DEV), 0)
+
+
+def test_tcmatmul_autograd_two_terms():
+    from face_b200.ops import Dense, TCMatmul
+    g = torch.Generator(device=DEV).manual_seed(2)
+    x1 = torch.randn(3, 777, 512, device=DEV, generator=g, requires_grad=True)
+    x2 = torch.randn(3, 777, 256, device=DEV, generator=g, requires_grad=True)
+    W1 = torch.randn(512, 64, device=DEV, generator=g) / 22
+    W2 = torch.randn(256, 64, device=DEV, generator=g) / 16
+    y = TCMatmul.apply(x1, Dense(W1), x2, Dense(W2))
+    G = torch.randn_like(y)
+    g1, g2 = torch.autograd.grad((y * G).sum(), (x1, x2))
+    X1, X2 = x1.double().detach(), x2.double().detach()
+    assert _rel(y, X1 @ W1.double() + X2 @ W2.double()) < 2e-6
+    assert _rel(g1, G.double() @ W1.double().t()) < 2e-6
+    assert _rel(g2, G.double() @ W2.double().t()) < 2e-6
+    assert _status() == 0

@@ -304,3 +304,34 @@ def test_pme_golden_fp64():
     assert abs(float(e) - float(k["recip_e"])) < 1e-12 * abs(float(k["recip_e"]))
     assert float((gp.cpu() - torch.tensor(k["recip_dpos"])).abs().max()) < 1e-11
     assert float((gq.cpu() - torch.tensor(k["recip_dq"])).abs().max()) < 1e-11
+
+
+def test_density_xm_bwd_fp32_ragged_rows():
+    """Flagship shape (B=16, K=32) in fp32 on CSR rows of degree 0..70 (empty rows included) through the C ABI,
+    against the same entry point in float64."""
+    from face_b200 import _lib
+    g = torch.Generator().manual_seed(8)
+    N = 3001
+    deg = torch.randint(0, 71, (N,), generator=g)
+    deg[::7] = 0
+    row_ptr = torch.zeros(N + 1, dtype=torch.int32)
+    row_ptr[1:] = torch.cumsum(deg, 0).to(torch.int32)
+    E = int(row_ptr[-1])
+    row_ptr = row_ptr.to(DEV)
+    phi = torch.randn(E, 16, generator=g, dtype=torch.float64).to(DEV)
+    msg = torch.randn(E, 32, generator=g, dtype=torch.float64).to(DEV)
+    Y = torch.randn(E, 20, generator=g, dtype=torch.float64).to(DEV)
+    Gs = [torch.randn(k, N, 512, generator=g, dtype=torch.float64).to(DEV) for k in (1, 3, 6, 10)]
+    out = {}
+    for dt in (torch.float64, torch.float32):
+        a = [t.to(dt).contiguous() for t in (phi, msg, Y)]
+        G = [t.to(dt).contiguous() for t in Gs]
+        d = [torch.full((E, c), float("nan"), dtype=dt, device=DEV) for c in (16, 32, 20)]
+        p = _lib.ptr
+        _lib.call("facek_density_xm_bwd", _lib.dtype_tag(a[0]), *[p(t) for t in a], *[p(t) for t in G],
+                  *[p(t) for t in d], N, 16, 32, p(row_ptr), _lib.stream())
+        torch.cuda.synchronize()
+        out[dt] = d
+    for u, v in zip(out[torch.float32], out[torch.float64]):
+        assert torch.isfinite(u).all()
+        assert rel(u.double(), v) < 1e-5
