@@ -5,21 +5,29 @@
 //
 // fp32 accuracy on the tf32 datapath through the 3-term split (tc.cuh). W is constant during a step, so it is
 // packed once (facek_gemm_pack) into an "image": for every N tile (Nt columns) and every 32-wide K chunk, a tf32
-// hi plane and a lo plane in the K-major operand layout. A is streamed from HBM by cp.async straight into the
-// K-major operand layout through a ring of S stages; that raw fp32 plane is the hi operand as the tensor core
-// reads it (low mantissa bits ignored), and the CTA writes only the lo plane x - trunc(x) (double-buffered).
-// One thread issues 4 K-steps x 3 split terms of M=128 x N=Nt x K=8 MMAs into TMEM.
+// hi plane and a lo plane in the K-major no-swizzle operand layout.
 //
+// Warp roles (352 threads; each single-thread role has a warp of its own so that no role's waits stall another):
+//   warp 8, lane 0     A producer: per K chunk one TMA 2D load of the 128 x 32 fp32 A tile into a 128-byte-
+//                      swizzled K-major stage of a deep ring (the hi operand as the tensor core reads raw fp32);
+//   warp 9, lane 0     W producer: one bulk copy of the chunk's W image into a shallow ring (L2-resident data);
+//                      stages complete on "full" mbarriers and are reused after the MMAs that read them commit
+//                      to their "empty" mbarriers, so the HBM stream runs SA - 1 chunks ahead of the MMAs.
+//   warp 10, lane 0    MMA issuer: once all 256 compute threads have arrived on the chunk's "split" mbarrier and
+//                      its W chunk has landed, 4 K-steps x 3 split terms of M=128 x N=Nt x K=8 MMAs into one of
+//                      three TMEM partials, then commits to the partial's, the A stage's and the W stage's
+//                      mbarriers.
+//   warps 0-7          split: lo = tf32(x - trunc(x)) into one of three lo planes (same swizzle), arrive; the
+//                      partial of the chunk two behind is loaded from TMEM while the split runs and folded into
+//                      fp32 registers; finished tiles are stored.  No block-wide barrier per chunk.
 // The tensor core accumulates in fp32 with truncation, so a long chain of MMAs into one accumulator drifts toward
-// zero. Each K chunk therefore starts a fresh TMEM partial (two alternate), and the CTA adds the partials in fp32
-// registers with round-to-nearest; the truncating chain is one chunk (12 MMAs) long whatever K is. Both
-// warpgroups read the partial back (half the columns each); the epilogue adds the bias and, for beta = 1, the
-// previous C.
+// zero; each K chunk therefore starts a fresh TMEM partial (three rotate) and the partials are summed in
+// registers with round-to-nearest (the truncating chain is 12 MMAs long whatever K is).
 //
-// CTAs are persistent over (M tile, N tile) units (consecutive units share the A tile, so its re-reads hit L2);
-// the chunk sequence runs across units so the ring keeps prefetching through the epilogue. Two mbarriers
-// alternate between consecutive chunks' commits, which keeps every parity wait unambiguous (no barrier is ever
-// two phases ahead of its waiter).
+// CTAs are persistent over (M tile, N tile) units (consecutive units share the A tile, so its re-reads hit L2).
+// Every mbarrier wait is bounded and parity-safe: no barrier is ever two phases ahead of a waiter.
+#include <cuda.h>
+
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -29,22 +37,13 @@ namespace {
 using namespace tc;
 
 constexpr int kM = 128;                       // rows per tile (MMA M)
-constexpr int kKc = 32;                       // K chunk (fp32 elements)
-constexpr int kThr = 256;
+constexpr int kKc = 32;                       // K chunk (fp32 elements) = one 128-byte swizzle row
+constexpr int kCompute = 256;                 // warps 0-7
+constexpr int kThr = kCompute + 96;           // + A producer, W producer and MMA issuer warps
 constexpr uint32_t kPlane = kM * kKc * 4;     // one 128 x 32 fp32 operand plane (16 KB)
 
-__device__ __forceinline__ void cp_async16_zfill(void* smem, const void* gmem, uint32_t src_bytes) {
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;\n" ::"r"(smem_u32(smem)), "l"(gmem), "r"(src_bytes)
-               : "memory");
-}
-template <int N>
-__device__ __forceinline__ void cp_async_wait_n() {
-  asm volatile("cp.async.wait_group %0;\n" ::"n"(N) : "memory");
-}
-
 struct GemmArgs {
-  const float* A;
-  int64_t M, K, lda;
+  int64_t M, K;
   const float* img;           // [n_tiles][k_chunks][hi|lo][Nt x kKc]
   int64_t N;
   int Nt, n_tiles, k_chunks;
@@ -55,12 +54,47 @@ struct GemmArgs {
   uint32_t tmem_cols;
 };
 
-// ring depth per N tile (H16 = Nt / 32 sixteen-column groups per warpgroup): S stages of [A | B hi | B lo] plus
-// the two lo planes fill the 227 KB opt-in shared memory of sm_100
+// Shared memory per N tile (H16 = Nt / 32): a deep ring of SA A tiles (the only HBM stream), a shallow ring of SW
+// W chunks (hi + lo, L2-resident), kLo lo planes; with 1 KB alignment slack this fills the 227 KB opt-in shared
+// memory of sm_100.
 template <int H16>
 struct Ring {
-  static constexpr int S = H16 == 1 ? 8 : H16 == 2 ? 6 : H16 <= 4 ? 4 : 3;
+  static constexpr int SA = H16 == 1 ? 9 : H16 <= 3 ? 7 : 6;
+  static constexpr int SW = H16 == 1 ? 3 : H16 == 2 ? 3 : 2;
 };
+constexpr int kLag = 2;                       // a chunk's TMEM partial is folded kLag iterations after its MMAs
+constexpr int kNB = kLag + 1;                 // TMEM partials and lo planes in rotation
+
+// byte offset of the 16-byte quad q of row r in a 128-byte-swizzled K-major plane (1024-byte aligned)
+__device__ __forceinline__ uint32_t sw128(uint32_t r, uint32_t q) { return r * 128u + ((q ^ (r & 7u)) << 4); }
+
+// shared-memory descriptor, K-major, 128-byte swizzle: 8-row atoms of 1024 B (SBO), LBO unused (1)
+__device__ __forceinline__ uint64_t desc_sw128(uint32_t saddr) {
+  uint64_t d = (uint64_t)((saddr >> 4) & 0x3FFFu);
+  d |= (uint64_t)1u << 16;
+  d |= (uint64_t)(1024u >> 4) << 32;
+  d |= (uint64_t)1u << 46;
+  d |= (uint64_t)2u << 61;
+  return d;
+}
+
+__device__ __forceinline__ void mbar_expect_tx(uint64_t* mbar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(mbar)), "r"(bytes)
+               : "memory");
+}
+__device__ __forceinline__ void tma_load_2d(void* dst, const CUtensorMap* map, int x, int y, uint64_t* mbar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+          smem_u32(dst)),
+      "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(mbar))
+      : "memory");
+}
+__device__ __forceinline__ void bulk_load(void* dst, const void* src, uint32_t bytes, uint64_t* mbar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(mbar))
+               : "memory");
+}
 
 // position of a chunk in the CTA's work: tile (mt, nt) and K chunk kc; advanced without divisions per chunk
 struct Cursor {
@@ -73,83 +107,56 @@ struct Cursor {
     mt = u / (uint32_t)n_tiles;
     nt = (int)(u % (uint32_t)n_tiles);
   }
-  // returns true when the step enters a new tile
-  __device__ bool next(int k_chunks, int n_tiles, uint32_t stride) {
-    if (++kc < k_chunks) return false;
+  __device__ void next(int k_chunks, int n_tiles, uint32_t stride) {
+    if (++kc < k_chunks) return;
     start(u + stride, n_tiles);
-    return true;
   }
 };
 
+__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(mbar)) : "memory");
+}
+
 template <int H16>
-__global__ void __launch_bounds__(kThr, 1) gemm_tc_k(GemmArgs g) {
-  constexpr int S = Ring<H16>::S;
+__global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUtensorMap amap, GemmArgs g) {
+  constexpr int SA = Ring<H16>::SA, SW = Ring<H16>::SW;
   constexpr int Nt = 32 * H16;
-  constexpr int HALF = Nt / 2;                                 // columns per warpgroup
-  constexpr uint32_t sb = kPlane + 2u * Nt * kKc * 4;          // stage: A (canonical, = hi operand) | B hi | B lo
-  constexpr uint32_t img_chunk = 2u * Nt * kKc;                // floats per (n tile, k chunk)
-  extern __shared__ __align__(1024) unsigned char sm[];
-  unsigned char* ring = sm;
-  unsigned char* lo_planes = sm + S * sb;                      // 2 x A lo
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(lo_planes + 2 * kPlane);
-  uint32_t* slot = reinterpret_cast<uint32_t*>(mbar + 2);
+  constexpr int HALF = Nt / 2;                                 // columns per compute warpgroup
+  constexpr uint32_t wbytes = 2u * Nt * kKc * 4;               // W hi + lo of one chunk
+  extern __shared__ unsigned char sm_raw[];
+  unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);   // 1024-byte aligned
+  unsigned char* aring = sm;                                   // SA x A tile (swizzled; = hi operand)
+  unsigned char* lo_planes = aring + SA * kPlane;              // kNB x A lo (same swizzle)
+  unsigned char* wring = lo_planes + kNB * kPlane;             // SW x [W hi | W lo]
+  uint64_t* fullA = reinterpret_cast<uint64_t*>(wring + SW * wbytes);
+  uint64_t* emptyA = fullA + SA;
+  uint64_t* fullW = emptyA + SA;
+  uint64_t* emptyW = fullW + SW;
+  uint64_t* mma_bar = emptyW + SW;                             // [kNB] MMAs of chunk j done (partial j % kNB)
+  uint64_t* split_bar = mma_bar + kNB;                         // [kNB] lo plane j % kNB written (256 arrivals)
+  uint32_t* slot = reinterpret_cast<uint32_t*>(split_bar + kNB);
   int* abort_ = reinterpret_cast<int*>(slot + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, wg = tid >> 7, row = tid & (kM - 1);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31, wg = (tid >> 7) & 1, row = tid & (kM - 1);
   const uint32_t m_tiles = (uint32_t)((g.M + kM - 1) / kM);
   const uint32_t units = m_tiles * (uint32_t)g.n_tiles;
   const uint32_t my_units = blockIdx.x < units ? (units - 1 - blockIdx.x) / gridDim.x + 1 : 0;
   const int64_t total = (int64_t)my_units * g.k_chunks;
 
-  // ---- producer mapping: lane -> row (lane & 7) of an 8-row group, 16-byte column quad (lane >> 3) + 4h;
-  // per warp-instruction 8 rows x 64 contiguous bytes (full sectors), and each 8-lane phase writes 8 distinct
-  // rows of one core matrix (conflict-free)
-  int p_row[4], p_col[4];
-  uint32_t p_off[4];
-#pragma unroll
-  for (int i = 0; i < 4; i++) {
-    const int grp = warp * 2 + (i & 1), h = i >> 1;
-    p_row[i] = grp * 8 + (lane & 7);
-    p_col[i] = ((lane >> 3) + 4 * h) * 4;
-    p_off[i] = kmajor_off(p_row[i], p_col[i], kM);
-  }
-  Cursor pc;                                                   // producer cursor
-  pc.start(blockIdx.x, g.n_tiles);
-  const float* p_src[4];
-  bool p_ok[4];
-  auto p_rows = [&]() {
-#pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const int64_t gr = pc.mt * kM + p_row[i];
-      p_ok[i] = gr < g.M;
-      p_src[i] = g.A + (p_ok[i] ? gr : 0) * g.lda + p_col[i];
-    }
-  };
-  p_rows();
-  int64_t p_next = 0;                                          // next chunk index to prefetch
-  auto prefetch = [&]() {
-    if (p_next < total) {
-      unsigned char* st = ring + (uint32_t)(p_next % S) * sb;
-      const int64_t k0 = (int64_t)pc.kc * kKc;
-#pragma unroll
-      for (int i = 0; i < 4; i++) {
-        const bool ok = p_ok[i] && k0 + p_col[i] < g.K;
-        cp_async16_zfill(st + p_off[i], ok ? p_src[i] + k0 : g.A, ok ? 16u : 0u);
-      }
-      const float* src = g.img + ((int64_t)pc.nt * g.k_chunks + pc.kc) * img_chunk;
-      unsigned char* dst = st + kPlane;
-#pragma unroll
-      for (int q = tid; q < (int)(img_chunk / 4); q += kThr) cp_async16_zfill(dst + q * 16, src + q * 4, 16u);
-      if (pc.next(g.k_chunks, g.n_tiles, gridDim.x)) p_rows();
-    }
-    p_next++;
-    asm volatile("cp.async.commit_group;\n" ::: "memory");     // one group per chunk slot, also past the end
-  };
-
   if (tid == 0) {
     *abort_ = 0;
-    mbar_init(&mbar[0], 1);
-    mbar_init(&mbar[1], 1);
+    for (int s = 0; s < SA; s++) {
+      mbar_init(&fullA[s], 1);
+      mbar_init(&emptyA[s], 1);
+    }
+    for (int s = 0; s < SW; s++) {
+      mbar_init(&fullW[s], 1);
+      mbar_init(&emptyW[s], 1);
+    }
+    for (int b = 0; b < kNB; b++) {
+      mbar_init(&mma_bar[b], 1);
+      mbar_init(&split_bar[b], kCompute);
+    }
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -161,109 +168,143 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(GemmArgs g) {
   fence_after_sync();
   const uint32_t tbase = *slot;
   volatile int* ab = abort_;
-  const uint32_t idesc = idesc_tf32(kM, Nt);
-  const uint32_t tl = tbase + ((uint32_t)((warp & 3) * 32) << 16) + wg * HALF;
 
-  // wait for the MMAs of chunk t (commits alternate between the two barriers, chunk t writes TMEM buffer t & 1)
-  auto wait_mma = [&](int64_t t) { mbar_wait(&mbar[t & 1], (uint32_t)((t >> 1) & 1), ab); };
-
-  float acc[HALF];
+  if (warp >= 8) {
+    if (warp == 8 && lane == 0) {
+      // ---------------------------------------------------------------- A producer (TMA, deep ring)
+      asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
+      Cursor pc;
+      pc.start(blockIdx.x, g.n_tiles);
+      for (int64_t j = 0; j < total; j++) {
+        const int s = (int)(j % SA);
+        if (j >= SA && !mbar_wait(&emptyA[s], (uint32_t)(((j / SA) - 1) & 1), ab)) break;
+        mbar_expect_tx(&fullA[s], kPlane);
+        tma_load_2d(aring + (uint32_t)s * kPlane, &amap, pc.kc * kKc, (int)(pc.mt * kM), &fullA[s]);
+        pc.next(g.k_chunks, g.n_tiles, gridDim.x);
+      }
+    } else if (warp == 9 && lane == 0) {
+      // ---------------------------------------------------------------- W producer (bulk copies, shallow ring)
+      Cursor pc;
+      pc.start(blockIdx.x, g.n_tiles);
+      for (int64_t j = 0; j < total; j++) {
+        const int s = (int)(j % SW);
+        if (j >= SW && !mbar_wait(&emptyW[s], (uint32_t)(((j / SW) - 1) & 1), ab)) break;
+        mbar_expect_tx(&fullW[s], wbytes);
+        bulk_load(wring + (uint32_t)s * wbytes, g.img + ((int64_t)pc.nt * g.k_chunks + pc.kc) * (wbytes / 4), wbytes,
+                  &fullW[s]);
+        pc.next(g.k_chunks, g.n_tiles, gridDim.x);
+      }
+    } else if (warp == 10 && lane == 0) {
+      // ---------------------------------------------------------------- MMA issuer
+      const uint32_t idesc = idesc_tf32(kM, Nt);
+      for (int64_t j = 0; j < total; j++) {
+        const int sa = (int)(j % SA), sw = (int)(j % SW), b = (int)(j % kNB);
+        if (!mbar_wait(&fullA[sa], (uint32_t)((j / SA) & 1), ab)) break;       // A tile landed (TMA)
+        if (!mbar_wait(&split_bar[b], (uint32_t)((j / kNB) & 1), ab)) break;   // lo plane written
+        if (!mbar_wait(&fullW[sw], (uint32_t)((j / SW) & 1), ab)) break;       // W chunk landed
+        fence_after_sync();
+        const uint32_t ah = smem_u32(aring + (uint32_t)sa * kPlane), al = smem_u32(lo_planes + (uint32_t)b * kPlane);
+        const uint32_t bh = smem_u32(wring + (uint32_t)sw * wbytes), bl = bh + Nt * kKc * 4;
+        const uint32_t dst = tbase + (uint32_t)b * Nt;
 #pragma unroll
-  for (int c = 0; c < HALF; c++) acc[c] = 0.f;
-  Cursor dc;                                                   // drain cursor (one chunk behind the MMAs)
-  dc.start(blockIdx.x, g.n_tiles);
-
-  // fold chunk t's partial into acc; store the tile when t is its last chunk
-  auto drain = [&](int64_t t) {
-    wait_mma(t);
-    fence_after_sync();
-    const uint32_t src = tl + (uint32_t)(t & 1) * Nt;
+        for (int k = 0; k < kKc / 8; k++) {
+          const uint64_t dah = desc_sw128(ah + k * 32), dal = desc_sw128(al + k * 32);
+          const uint64_t dbh = desc_kmajor(bh + k * 2 * Nt * 16, Nt * 16, 128);
+          const uint64_t dbl = desc_kmajor(bl + k * 2 * Nt * 16, Nt * 16, 128);
+          mma_tf32(dst, dal, dbh, idesc, k > 0 ? 1u : 0u);     // small terms first
+          mma_tf32(dst, dah, dbl, idesc, 1u);
+          mma_tf32(dst, dah, dbh, idesc, 1u);
+        }
+        commit(&mma_bar[b]);
+        commit(&emptyA[sa]);
+        commit(&emptyW[sw]);
+      }
+    }
+  } else {
+    // ------------------------------------------------------------------ compute warps (no block-wide barrier)
+    const uint32_t tl = tbase + ((uint32_t)((warp & 3) * 32) << 16) + wg * HALF;
+    float acc[HALF];
 #pragma unroll
-    for (int c0 = 0; c0 < HALF; c0 += 16) {
-      float v[16];
-      tmem_ld16(src + c0, v);
+    for (int c = 0; c < HALF; c++) acc[c] = 0.f;
+    Cursor dc;                                                 // drain cursor (kLag chunks behind the split)
+    dc.start(blockIdx.x, g.n_tiles);
+
+    // chunk t's partial: wait for its MMAs and start the TMEM loads (completed by drain_finish)
+    float part[HALF];
+    auto drain_start = [&](int64_t t) -> bool {
+      if (!mbar_wait(&mma_bar[t % kNB], (uint32_t)((t / kNB) & 1), ab)) return false;
+      fence_after_sync();
+      const uint32_t src = tl + (uint32_t)(t % kNB) * Nt;
+#pragma unroll
+      for (int c0 = 0; c0 < HALF; c0 += 16) tmem_ld16(src + c0, part + c0);
+      return true;
+    };
+    // fold it into acc; store the tile when t is its last chunk
+    auto drain_finish = [&]() {
       tmem_wait_ld();
 #pragma unroll
-      for (int q = 0; q < 16; q++) acc[c0 + q] += v[q];
-    }
-    fence_before_sync();
-    if (dc.kc == g.k_chunks - 1) {
-      const int64_t grow = dc.mt * kM + row;
-      const int64_t gc0 = (int64_t)dc.nt * Nt + wg * HALF;
-      if (grow < g.M) {
-        float* out = g.C + grow * g.ldc + gc0;
+      for (int q = 0; q < HALF; q++) acc[q] += part[q];
+      fence_before_sync();
+      if (dc.kc == g.k_chunks - 1) {
+        const int64_t grow = dc.mt * kM + row;
+        const int64_t gc0 = (int64_t)dc.nt * Nt + wg * HALF;
+        if (grow < g.M) {
+          float* out = g.C + grow * g.ldc + gc0;
 #pragma unroll
-        for (int q = 0; q < HALF; q += 4) {
-          if (gc0 + q < g.N) {
-            float4 o = make_float4(acc[q], acc[q + 1], acc[q + 2], acc[q + 3]);
-            if (g.bias) {
-              o.x += g.bias[gc0 + q];
-              o.y += g.bias[gc0 + q + 1];
-              o.z += g.bias[gc0 + q + 2];
-              o.w += g.bias[gc0 + q + 3];
+          for (int q = 0; q < HALF; q += 4) {
+            if (gc0 + q < g.N) {
+              float4 o = make_float4(acc[q], acc[q + 1], acc[q + 2], acc[q + 3]);
+              if (g.bias) {
+                o.x += g.bias[gc0 + q];
+                o.y += g.bias[gc0 + q + 1];
+                o.z += g.bias[gc0 + q + 2];
+                o.w += g.bias[gc0 + q + 3];
+              }
+              if (g.beta) {
+                const float4 p = *reinterpret_cast<const float4*>(out + q);
+                o.x += p.x;
+                o.y += p.y;
+                o.z += p.z;
+                o.w += p.w;
+              }
+              *reinterpret_cast<float4*>(out + q) = o;
             }
-            if (g.beta) {
-              const float4 p = *reinterpret_cast<const float4*>(out + q);
-              o.x += p.x;
-              o.y += p.y;
-              o.z += p.z;
-              o.w += p.w;
-            }
-            *reinterpret_cast<float4*>(out + q) = o;
           }
         }
+#pragma unroll
+        for (int c = 0; c < HALF; c++) acc[c] = 0.f;
       }
-#pragma unroll
-      for (int c = 0; c < HALF; c++) acc[c] = 0.f;
-    }
-    dc.next(g.k_chunks, g.n_tiles, gridDim.x);
-  };
+      dc.next(g.k_chunks, g.n_tiles, gridDim.x);
+    };
 
-#pragma unroll 1
-  for (int s = 0; s < S - 1; s++) prefetch();
-
-  for (int64_t j = 0; j < total; j++) {
-    cp_async_wait_n<S - 2>();                                  // chunk j has landed (this thread's copies)
-    fence_proxy_async_smem();
-    __syncthreads();                                           // ... and every thread's
-    if (*ab) break;                                            // uniform: read between two barriers
-    unsigned char* st = ring + (uint32_t)(j % S) * sb;
-    unsigned char* lo = lo_planes + (uint32_t)(j & 1) * kPlane;
-    // lo plane: x - trunc(x) rounded to tf32; thread owns one row, 4 of the 8 column quads
+    bool ok = true;
+    for (int64_t j = 0; j < total && ok; j++) {
+      const int sa = (int)(j % SA), b = (int)(j % kNB);
+      const int64_t t = j - kLag;                               // chunk drained in this iteration
+      // draining chunk j - kLag also proves lo plane b free: MMA(j - kNB) completed before MMA(j - kLag)
+      if (t >= 0 && !(ok = drain_start(t))) break;
+      if (!(ok = mbar_wait(&fullA[sa], (uint32_t)((j / SA) & 1), ab))) break;   // A tile landed
+      const unsigned char* at = aring + (uint32_t)sa * kPlane;
+      unsigned char* lo = lo_planes + (uint32_t)b * kPlane;
+      // lo plane: x - trunc(x) rounded to tf32; thread owns one row, 4 of the 8 16-byte quads
 #pragma unroll
-    for (int i = 0; i < 4; i++) {
-      const uint32_t off = kmajor_off(row, (wg * 4 + i) * 4, kM);
-      const float4 v = *reinterpret_cast<const float4*>(st + off);
-      *reinterpret_cast<float4*>(lo + off) =
-          make_float4(to_tf32(v.x - tf32_trunc(v.x)), to_tf32(v.y - tf32_trunc(v.y)), to_tf32(v.z - tf32_trunc(v.z)),
-                      to_tf32(v.w - tf32_trunc(v.w)));
-    }
-    fence_proxy_async_smem();
-    fence_before_sync();
-    __syncthreads();
-    if (tid == 0) {
-      fence_after_sync();
-      const uint32_t ah = smem_u32(st), al = smem_u32(lo);
-      const uint32_t bh = ah + kPlane, bl = bh + Nt * kKc * 4;
-      const uint32_t dst = tbase + (uint32_t)(j & 1) * Nt;
-#pragma unroll
-      for (int s = 0; s < kKc / 8; s++) {
-        const uint64_t dah = desc_kmajor(ah + s * 2 * kM * 16, kM * 16, 128);
-        const uint64_t dal = desc_kmajor(al + s * 2 * kM * 16, kM * 16, 128);
-        const uint64_t dbh = desc_kmajor(bh + s * 2 * Nt * 16, Nt * 16, 128);
-        const uint64_t dbl = desc_kmajor(bl + s * 2 * Nt * 16, Nt * 16, 128);
-        mma_tf32(dst, dal, dbh, idesc, s > 0 ? 1u : 0u);       // small terms first
-        mma_tf32(dst, dah, dbl, idesc, 1u);
-        mma_tf32(dst, dah, dbh, idesc, 1u);
+      for (int i = 0; i < 4; i++) {
+        const uint32_t off = sw128(row, wg * 4 + i);
+        const float4 v = *reinterpret_cast<const float4*>(at + off);
+        *reinterpret_cast<float4*>(lo + off) =
+            make_float4(to_tf32(v.x - tf32_trunc(v.x)), to_tf32(v.y - tf32_trunc(v.y)),
+                        to_tf32(v.z - tf32_trunc(v.z)), to_tf32(v.w - tf32_trunc(v.w)));
       }
-      commit(&mbar[j & 1]);
+      if (t >= 0) drain_finish();
+      fence_proxy_async_smem();                                // lo writes -> async proxy, TMEM loads done
+      mbar_arrive(&split_bar[b]);
     }
-    // chunk j-1: its MMAs are done -> fold its partial, free ring stage (j-1)%S and lo plane (j+1)&1
-    if (j > 0) drain(j - 1);
-    prefetch();
+    if (ok && !*ab)
+      for (int64_t t = total - kLag > 0 ? total - kLag : 0; t < total; t++) {
+        if (!drain_start(t)) break;
+        drain_finish();
+      }
   }
-  if (!*ab && total > 0) drain(total - 1);
-  cp_async_wait_n<0>();
   fence_before_sync();
   __syncthreads();
   if (warp == 0) {
@@ -293,21 +334,39 @@ __global__ void gemm_pack_k(const float* __restrict__ W, int64_t K, int64_t N, i
 }
 
 int pick_nt(int64_t N) {
-  // N tile: a multiple of 32 (epilogue halves of 16-column loads) up to 192, so that two ring stages fit next to
-  // the operand buffers; wider N runs as 128-column tiles
-  const int64_t n32 = (N + 31) / 32 * 32;
-  return n32 <= 192 ? (int)n32 : 128;
+  // N tile: a multiple of 32 (epilogue halves of 16-column loads) up to 128 (four TMEM partials and three ring
+  // stages fit); wider N splits into equal tiles
+  const int64_t n32 = (N + 31) / 32;
+  const int64_t tiles = (n32 + 3) / 4;
+  return (int)((n32 + tiles - 1) / tiles) * 32;
+}
+
+typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
+                                  const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
+                                  CUtensorMapSwizzle, CUtensorMapL2promotion, CUtensorMapFloatOOBfill);
+
+EncodeTiledFn encode_fn() {
+  static EncodeTiledFn fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<EncodeTiledFn>(p);
+  }
+  return fn;
 }
 
 template <int H16>
-int launch_gemm(const GemmArgs& g, void* stream) {
+int launch_gemm(const CUtensorMap& amap, const GemmArgs& g, void* stream) {
   constexpr int Nt = 32 * H16;
-  const size_t smem = Ring<H16>::S * (kPlane + 2u * Nt * kKc * 4) + 2 * kPlane + 64;
+  constexpr int SA = Ring<H16>::SA, SW = Ring<H16>::SW;
+  const size_t smem = (SA + kNB) * kPlane + SW * (2u * Nt * kKc * 4) + (2 * SA + 2 * SW + 2 * kNB) * 8 + 16 + 1024;
   FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_gemm_tc: %zu B of shared memory needed", smem);
   cudaFuncSetAttribute(gemm_tc_k<H16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t units = ((g.M + kM - 1) / kM) * g.n_tiles;
   const int grid = (int)std::min<int64_t>(units, sm_count());
-  gemm_tc_k<H16><<<grid, kThr, smem, as_stream(stream)>>>(g);
+  gemm_tc_k<H16><<<grid, kThr, smem, as_stream(stream)>>>(amap, g);
   return launch_status("facek_gemm_tc");
 }
 
@@ -356,11 +415,21 @@ extern "C" int facek_gemm_tc(const float* A, int64_t M, int64_t K, int64_t lda, 
   FACEK_CHECK_ARG(N % 4 == 0 && ldc % 4 == 0 && ldc >= N && (reinterpret_cast<uintptr_t>(C) & 15) == 0,
                   "facek_gemm_tc: C needs N %% 4 == 0, ldc %% 4 == 0, ldc >= N and 16-byte alignment");
   FACEK_CHECK_ARG((reinterpret_cast<uintptr_t>(image) & 15) == 0, "facek_gemm_tc: image not 16-byte aligned");
+  FACEK_CHECK_ARG(M < (int64_t)1 << 31 && K < (int64_t)1 << 31, "facek_gemm_tc: M, K must be < 2^31");
+  EncodeTiledFn enc = encode_fn();
+  FACEK_CHECK_ARG(enc != nullptr, "facek_gemm_tc: cuTensorMapEncodeTiled unavailable");
+  CUtensorMap amap;
+  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
+  const cuuint64_t strides[1] = {(cuuint64_t)lda * 4};
+  const cuuint32_t box[2] = {(cuuint32_t)kKc, (cuuint32_t)kM};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult cr = enc(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(A), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FACEK_CHECK_ARG(cr == CUDA_SUCCESS, "facek_gemm_tc: tensor map encoding failed (%d)", (int)cr);
   GemmArgs g{};
-  g.A = A;
   g.M = M;
   g.K = K;
-  g.lda = lda;
   g.img = image;
   g.N = N;
   g.Nt = pick_nt(N);
@@ -371,14 +440,12 @@ extern "C" int facek_gemm_tc(const float* A, int64_t M, int64_t K, int64_t lda, 
   g.ldc = ldc;
   g.beta = beta ? 1 : 0;
   uint32_t cols = 32;
-  while (cols < 2u * (uint32_t)g.Nt) cols <<= 1;                // two chunk partials
+  while (cols < (uint32_t)(kNB * g.Nt)) cols <<= 1;             // kNB chunk partials
   g.tmem_cols = cols;
   switch (g.Nt / 32) {
-    case 1: return launch_gemm<1>(g, stream);
-    case 2: return launch_gemm<2>(g, stream);
-    case 3: return launch_gemm<3>(g, stream);
-    case 4: return launch_gemm<4>(g, stream);
-    case 5: return launch_gemm<5>(g, stream);
-    default: return launch_gemm<6>(g, stream);
+    case 1: return launch_gemm<1>(amap, g, stream);
+    case 2: return launch_gemm<2>(amap, g, stream);
+    case 3: return launch_gemm<3>(amap, g, stream);
+    default: return launch_gemm<4>(amap, g, stream);
   }
 }
