@@ -6,12 +6,15 @@
 //   a2    = silu(W2 a1 + b2)
 //   phi   = (W3 a2 + b3) * env(r),  dphi/dr by pushing d/dr through the same three layers
 //
-// One CTA = two warpgroups; each warpgroup owns a 128-edge tile (one edge per thread = one TMEM lane) and runs
+// One CTA = two groups of 8 warps; each group owns a 128-edge tile, two threads per edge (one TMEM lane, each
+// thread half of the 64 hidden units), and runs
 //   layer 1 on the CUDA cores -> W2 x [a1 | da1] on the tensor core -> silu epilogue -> W3 x [a2 | da2] on the
 //   tensor core -> phi, dphi/dr epilogue,
-// so one warpgroup's CUDA-core work overlaps the other's MMAs. The MMAs run kind::tf32 with the 3-term split,
+// so one group's CUDA-core work overlaps the other's MMAs (16 warps per SM hide the CUDA-core latencies).  The
+// pair embedding is kept transposed, [hidden][pair] with b1 folded in, so lanes with different element pairs read
+// different banks.  The MMAs run kind::tf32 with the 3-term split,
 // which keeps fp32 accuracy (tc.cuh). Weights are split once per CTA into shared memory; the CTA is persistent
-// over tiles. Tensor memory: 128 fp32 columns per warpgroup (value and tangent accumulators of W2, later reused
+// over tiles. Tensor memory: 128 fp32 columns per group (value and tangent accumulators of W2, later reused
 // for W3).
 #include "common.cuh"
 #include "radial.cuh"
@@ -24,7 +27,7 @@ using namespace tc;
 
 constexpr int kH = 64;                               // hidden width
 constexpr int kRows = 128;                           // edges per warpgroup tile = MMA M
-constexpr int kThreads = 256;                        // two warpgroups
+constexpr int kThreads = 512;                        // two groups of 8 warps (2 threads per edge row)
 constexpr uint32_t kPlane = kRows * kH * 4;          // one fp32 operand plane (32 KB)
 constexpr uint32_t kTmemCols = 256;
 
@@ -41,7 +44,7 @@ __host__ __device__ inline Layout layout_for(int NB, int BO, int n_el) {
   L.b1 = L.w1 + kH * NB * 4;
   L.b2 = L.b1 + kH * 4;
   L.b3 = L.b2 + kH * 4;
-  L.pair = L.b3 + BO * 4;                             // pair embedding (n_el^2 x 64)
+  L.pair = L.b3 + BO * 4;                             // b1 + pair embedding, transposed: [64][n_el^2]
   L.mbar = L.pair + n_el * n_el * kH * 4;             // 2 x 8 B
   L.slot = L.mbar + 16;
   L.abort_ = L.slot + 16;                             // 2 x 4 B
@@ -69,7 +72,9 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint32_t* slot = reinterpret_cast<uint32_t*>(sm + L.slot);
   int* abort_ = reinterpret_cast<int*>(sm + L.abort_);
 
-  const int tid = threadIdx.x, warp = tid >> 5, wg = tid >> 7, row = tid & (kRows - 1);
+  const int tid = threadIdx.x, warp = tid >> 5, wg = tid >> 8, wt = tid & 255, row = wt & (kRows - 1);
+  const int half = wt >> 7;                          // hidden units [32 half, 32 half + 32) of this thread's row
+  const int np = n_el * n_el;
 
   // ---- weights -> shared memory (W2, W3 as tf32 hi/lo planes in the K-major operand layout)
   for (int q = tid; q < kH * kH; q += kThreads) {
@@ -93,7 +98,10 @@ __global__ void __launch_bounds__(kThreads, 1)
     b2s[q] = b2[q];
   }
   for (int q = tid; q < BO; q += kThreads) b3s[q] = b3[q];
-  for (int q = tid; q < n_el * n_el * kH; q += kThreads) pairs[q] = pair[q];
+  for (int q = tid; q < np * kH; q += kThreads) {
+    const int pp = q / kH, h = q % kH;
+    pairs[h * np + pp] = pair[q] + b1[h];
+  }
   if (tid == 0) {
     abort_[0] = 0;
     abort_[1] = 0;
@@ -126,8 +134,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   auto round = [&](uint32_t dcol, uint32_t b_hi, uint32_t b_lo, uint32_t b_rows, uint32_t idesc) {
     fence_proxy_async_smem();
     fence_before_sync();
-    bar_sync(1 + wg, kRows);
-    if (row == 0 && !*ab) {
+    bar_sync(1 + wg, 2 * kRows);
+    if (wt == 0 && !*ab) {
       fence_after_sync();
 #pragma unroll
       for (int s = 0; s < kH / 8; s++) {
@@ -150,7 +158,7 @@ __global__ void __launch_bounds__(kThreads, 1)
   const float pi = 3.14159265358979323846f;
   const int64_t ntiles = (E + kRows - 1) / kRows;
   for (int64_t t = (int64_t)blockIdx.x * 2 + wg; t < ntiles; t += (int64_t)gridDim.x * 2) {
-    bar_sync(1 + wg, kRows);
+    bar_sync(1 + wg, 2 * kRows);
     if (*ab) break;                                  // uniform: nothing writes the flag between these points
     const int64_t e = t * kRows + row;
     const bool valid = e < E;
@@ -177,16 +185,18 @@ __global__ void __launch_bounds__(kThreads, 1)
         drb[n] = dbes * env + bes * denv;
       }
     }
-    // ---- layer 1 on the CUDA cores: a1 -> operand planes, da1 kept in registers
-    const float* prow = pairs + p * kH;
-    float da1[kH];
+    // ---- layer 1 on the CUDA cores (this thread's 32 hidden units): a1 -> operand planes, da1 in registers
+    const float* pcol = pairs + p;
+    constexpr int kHh = kH / 2;
+    float da1[kHh];
 #pragma unroll
-    for (int h0 = 0; h0 < kH; h0 += 4) {
+    for (int hh = 0; hh < kHh; hh += 4) {
+      const int h0 = half * kHh + hh;
       float a[4];
 #pragma unroll
       for (int j = 0; j < 4; j++) {
         const int h = h0 + j;
-        float z = b1s[h] + prow[h], dz = 0.f;
+        float z = pcol[h * np], dz = 0.f;
 #pragma unroll
         for (int n = 0; n < NB; n++) {
           z += w1s[h * NB + n] * rb[n];
@@ -194,20 +204,22 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         const float sg = sigmoid(z);
         a[j] = z * sg;
-        da1[h] = sg * (1.f + z * (1.f - sg)) * dz;
+        da1[hh + j] = sg * (1.f + z * (1.f - sg)) * dz;
       }
       store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), a[0], a[1], a[2], a[3]);
     }
     round(col0, w2_hi_s, w2_lo_s, kH, idesc_tf32(kRows, kH));                // z2 -> columns [0, 64)
 #pragma unroll
-    for (int h0 = 0; h0 < kH; h0 += 4)
-      store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), da1[h0], da1[h0 + 1], da1[h0 + 2], da1[h0 + 3]);
+    for (int hh = 0; hh < kHh; hh += 4)
+      store_split4(a_hi, a_lo, kmajor_off(row, half * kHh + hh, kRows), da1[hh], da1[hh + 1], da1[hh + 2],
+                   da1[hh + 3]);
     round(col0 + 64, w2_hi_s, w2_lo_s, kH, idesc_tf32(kRows, kH));           // dz2 -> columns [64, 128)
 
     // ---- silu epilogue of layer 2: a2 -> operand planes, da2 kept in registers
-    float da2[kH];
+    float da2[kHh];
 #pragma unroll
-    for (int c0 = 0; c0 < kH; c0 += 16) {
+    for (int cc = 0; cc < kHh; cc += 16) {
+      const int c0 = half * kHh + cc;
       float z[16], dz[16];
       tmem_ld16(tl + c0, z);
       tmem_ld16(tl + 64 + c0, dz);
@@ -218,7 +230,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const float zz = z[j] + b2s[c0 + j];
         const float sg = sigmoid(zz);
         a[j] = zz * sg;
-        da2[c0 + j] = sg * (1.f + zz * (1.f - sg)) * dz[j];
+        da2[cc + j] = sg * (1.f + zz * (1.f - sg)) * dz[j];
       }
 #pragma unroll
       for (int q = 0; q < 16; q += 4)
@@ -226,13 +238,14 @@ __global__ void __launch_bounds__(kThreads, 1)
     }
     round(col0, w3_hi_s, w3_lo_s, BO, idesc_tf32(kRows, BO));                // z3 -> columns [0, BO)
 #pragma unroll
-    for (int h0 = 0; h0 < kH; h0 += 4)
-      store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), da2[h0], da2[h0 + 1], da2[h0 + 2], da2[h0 + 3]);
+    for (int hh = 0; hh < kHh; hh += 4)
+      store_split4(a_hi, a_lo, kmajor_off(row, half * kHh + hh, kRows), da2[hh], da2[hh + 1], da2[hh + 2],
+                   da2[hh + 3]);
     round(col0 + 32, w3_hi_s, w3_lo_s, BO, idesc_tf32(kRows, BO));           // dz3 -> columns [32, 32 + BO)
 
-    // ---- output epilogue
+    // ---- output epilogue: 16-column groups split between the two halves (half 1 idle when BO = 16)
 #pragma unroll
-    for (int c0 = 0; c0 < BO; c0 += 16) {
+    for (int c0 = 16 * half; c0 < BO; c0 += 32) {
       float z[16], dz[16];
       tmem_ld16(tl + c0, z);
       tmem_ld16(tl + 32 + c0, dz);
