@@ -303,6 +303,97 @@ int launch_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*>
   return launch_status("facek_density_bwd");
 }
 
+// Backward, one lane per edge (fp32, B = 16, K = 32).  A 64-thread CTA takes one row (atom) at a time: it stages
+// the row's G (20 x 512 fp32, 40 KB) in shared memory with cp.async, then each lane walks the 320 rows (x, b) of
+// G for its edge with 128-byte broadcast reads (all lanes read the same address):
+//   t = sum_k msg[k] g[k]  ->  dphi[b] += t Y[x],  dY[x] += t phi[b],   dmsg[k] += Y[x] phi[b] g[k]
+// (2 K + 3 FMAs per 8 shared vector loads), msg and dmsg of the edge in registers.  Five CTAs share an SM, so
+// one CTA's staging overlaps the others' arithmetic.  Rows with more than 64 edges loop over lane blocks.
+template <int BB, int KK>
+__global__ void __launch_bounds__(64, 5) dens_bwd_lane_k(const float* __restrict__ phi, const float* __restrict__ msg,
+                                                         const float* __restrict__ Y, Planes<const float*> G,
+                                                         float* __restrict__ dphi, float* __restrict__ dmsg,
+                                                         float* __restrict__ dY, int64_t N, Rows rows) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* sG = reinterpret_cast<float*>(smem_raw);              // [x][b][k]
+  constexpr int BK = BB * KK;
+  const int tid = threadIdx.x;
+  for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
+    int64_t e0;
+    int deg;
+    rows.range(i, e0, deg);
+    if (deg == 0) continue;
+    __syncthreads();                                           // previous row's readers are done with sG
+#pragma unroll 4
+    for (int x = 0; x < NX; x++) stage(sG + x * BK, G.at(i, x), BK, tid, 64);
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    for (int t0 = 0; t0 < deg; t0 += 64) {
+      if (t0 + tid >= deg) break;
+      const int64_t e = e0 + t0 + tid;
+      float m[KK], dm[KK], p[BB], dp[BB];
+#pragma unroll
+      for (int k = 0; k < KK; k += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(msg + e * KK + k));
+        m[k] = v.x;
+        m[k + 1] = v.y;
+        m[k + 2] = v.z;
+        m[k + 3] = v.w;
+        dm[k] = dm[k + 1] = dm[k + 2] = dm[k + 3] = 0.f;
+      }
+#pragma unroll
+      for (int b = 0; b < BB; b += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(phi + e * BB + b));
+        p[b] = v.x;
+        p[b + 1] = v.y;
+        p[b + 2] = v.z;
+        p[b + 3] = v.w;
+        dp[b] = dp[b + 1] = dp[b + 2] = dp[b + 3] = 0.f;
+      }
+#pragma unroll 1
+      for (int x = 0; x < NX; x++) {
+        const float yx = __ldg(Y + e * NX + x);
+        const float* gx = sG + x * BK;
+        float dyx = 0.f;
+#pragma unroll
+        for (int b = 0; b < BB; b++) {
+          float g[KK];
+#pragma unroll
+          for (int k = 0; k < KK; k += 4) {
+            const float4 v = *reinterpret_cast<const float4*>(gx + b * KK + k);
+            g[k] = v.x;
+            g[k + 1] = v.y;
+            g[k + 2] = v.z;
+            g[k + 3] = v.w;
+          }
+          float t0_ = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+#pragma unroll
+          for (int k = 0; k < KK; k += 4) {
+            t0_ += m[k] * g[k];
+            t1 += m[k + 1] * g[k + 1];
+            t2 += m[k + 2] * g[k + 2];
+            t3 += m[k + 3] * g[k + 3];
+          }
+          const float t = (t0_ + t1) + (t2 + t3);
+          dp[b] += t * yx;
+          dyx += t * p[b];
+          const float w = yx * p[b];
+#pragma unroll
+          for (int k = 0; k < KK; k++) dm[k] += w * g[k];
+        }
+        dY[e * NX + x] = dyx;
+      }
+#pragma unroll
+      for (int b = 0; b < BB; b += 4)
+        *reinterpret_cast<float4*>(dphi + e * BB + b) = make_float4(dp[b], dp[b + 1], dp[b + 2], dp[b + 3]);
+#pragma unroll
+      for (int k = 0; k < KK; k += 4)
+        *reinterpret_cast<float4*>(dmsg + e * KK + k) = make_float4(dm[k], dm[k + 1], dm[k + 2], dm[k + 3]);
+    }
+  }
+}
+
 template <typename T>
 int density_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*> G, void* dphi, void* dmsg,
                 void* dY, int64_t N, int M, int B, int K, const int32_t* row_ptr, void* stream) {
@@ -310,6 +401,13 @@ int density_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*
   Rows rows{row_ptr, M};
   FACEK_CHECK_ARG(B <= 32, "facek_density_bwd: B=%d > 32 unsupported", B);
   if constexpr (sizeof(T) == 4) {
+    if (B == 16 && K == 32) {                          // flagship shape: lane-per-edge kernel, G in shared memory
+      const size_t smem = sizeof(float) * NX * 16 * 32;
+      cudaFuncSetAttribute(dens_bwd_lane_k<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      dens_bwd_lane_k<16, 32><<<grid_for(N, 5), 64, smem, as_stream(stream)>>>(
+          (const float*)phi, (const float*)msg, (const float*)Y, G, (float*)dphi, (float*)dmsg, (float*)dY, N, rows);
+      return launch_status("facek_density_bwd");
+    }
     if (B <= 16) return launch_bwd<T, 8, 16>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
     return launch_bwd<T, 8, 32>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
   } else {
