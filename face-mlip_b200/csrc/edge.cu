@@ -594,6 +594,144 @@ __global__ void __launch_bounds__(256) transport_bwd_k(const T* __restrict__ phi
   }
 }
 
+// Transport backward, one lane per edge (fp32, B = BB, Kd a multiple of 4).  A 64-thread CTA takes one row (atom)
+// at a time and stages its 18 gradient rows dT[o, i] (BB x Kd each) in shared memory.  For each group of 4 kd
+// channels a lane keeps g = Gt[:, j, kd..kd+3] (9 x 4), walks the 18 outputs o and for each the BB rows
+// dT[o, i, b, kd..kd+3] (16-byte broadcast reads):
+//   dphi[b] += dT . f_o,   P_o = sum_b phi[b] dT   ->   folded at once into dV, dM (per kd) and du
+// Same outputs as transport_bwd_k.  Rows with more than 64 edges loop over lane blocks.
+template <int BB>
+__global__ void __launch_bounds__(64, 8) transport_bwd_lane_k(const float* __restrict__ phi,
+                                                              const float* __restrict__ vec,
+                                                              const int32_t* __restrict__ ej,
+                                                              const float* __restrict__ Gt,
+                                                              const float* __restrict__ dT1,
+                                                              const float* __restrict__ dT2,
+                                                              const int32_t* __restrict__ row_ptr,
+                                                              float* __restrict__ dphi, float* __restrict__ dvec,
+                                                              int acc, float* __restrict__ dGe, int64_t N, int Kd) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  float* sD = reinterpret_cast<float*>(smem_raw);              // [o][b][kd], o in output order
+  const int tid = threadIdx.x;
+  const int BKd = BB * Kd;
+  for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
+    const int64_t e0 = row_ptr[i];
+    const int deg = row_ptr[i + 1] - (int)e0;
+    if (deg == 0) continue;
+    __syncthreads();                                           // previous row's readers are done with sD
+#pragma unroll 2
+    for (int o = 0; o < 18; o++) {
+      const int64_t off = plane_off(trow(o), i, N, BKd);
+      stage(sD + o * BKd, trow(o) < 6 ? dT1 + off : dT2 + (off - 6 * N * (int64_t)BKd), BKd, tid, 64);
+    }
+    cp_async_commit();
+    cp_async_wait<0>();
+    __syncthreads();
+    for (int t0 = 0; t0 < deg; t0 += 64) {
+      if (t0 + tid >= deg) break;
+      const int64_t e = e0 + t0 + tid, j = ej[e];
+      const float vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+      const float r = sqrtf(vx * vx + vy * vy + vz * vz);
+      const float u[3] = {vx / r, vy / r, vz / r};
+      float p[BB], dp[BB];
+#pragma unroll
+      for (int b = 0; b < BB; b += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(phi + e * BB + b));
+        p[b] = v.x;
+        p[b + 1] = v.y;
+        p[b + 2] = v.z;
+        p[b + 3] = v.w;
+        dp[b] = dp[b + 1] = dp[b + 2] = dp[b + 3] = 0.f;
+      }
+      float du[3] = {0.f, 0.f, 0.f};
+#pragma unroll 1
+      for (int k0 = 0; k0 < Kd; k0 += 4) {
+        float g[9][4], dG[9][4];
+#pragma unroll
+        for (int c = 0; c < 9; c++) {
+          const float4 v = __ldg(reinterpret_cast<const float4*>(Gt + ((int64_t)c * N + j) * Kd + k0));
+          g[c][0] = v.x;
+          g[c][1] = v.y;
+          g[c][2] = v.z;
+          g[c][3] = v.w;
+#pragma unroll
+          for (int q = 0; q < 4; q++) dG[c][q] = 0.f;
+        }
+#pragma unroll
+        for (int o = 0; o < 18; o++) {
+          float f[4];
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            if (o < 3) f[q] = g[o][q];
+            else if (o < 6) {
+              const int a = o - 3;
+              f[q] = g[3 + s2i(a, 0)][q] * u[0] + g[3 + s2i(a, 1)][q] * u[1] + g[3 + s2i(a, 2)][q] * u[2];
+            } else if (o < 12) f[q] = g[3 + (o - 6)][q];
+            else {
+              const int s = o - 12, pp = pair_p(s), qq = pair_q(s);
+              f[q] = pp == qq ? u[pp] * g[pp][q] : 0.5f * (u[pp] * g[qq][q] + u[qq] * g[pp][q]);
+            }
+          }
+          const float* rowp = sD + o * BKd + k0;
+          float P[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+          for (int b = 0; b < BB; b++) {
+            const float4 d = *reinterpret_cast<const float4*>(rowp + b * Kd);
+            dp[b] += (d.x * f[0] + d.y * f[1]) + (d.z * f[2] + d.w * f[3]);
+            P[0] += p[b] * d.x;
+            P[1] += p[b] * d.y;
+            P[2] += p[b] * d.z;
+            P[3] += p[b] * d.w;
+          }
+#pragma unroll
+          for (int q = 0; q < 4; q++) {
+            const float w = P[q];
+            if (o < 3) dG[o][q] += w;
+            else if (o < 6) {
+              const int a = o - 3;
+#pragma unroll
+              for (int bb = 0; bb < 3; bb++) {
+                dG[3 + s2i(a, bb)][q] += w * u[bb];
+                du[bb] += w * g[3 + s2i(a, bb)][q];
+              }
+            } else if (o < 12) dG[3 + (o - 6)][q] += w;
+            else {
+              const int s = o - 12, pp = pair_p(s), qq = pair_q(s);
+              if (pp == qq) {
+                du[pp] += w * g[pp][q];
+                dG[pp][q] += w * u[pp];
+              } else {
+                du[pp] += 0.5f * w * g[qq][q];
+                du[qq] += 0.5f * w * g[pp][q];
+                dG[qq][q] += 0.5f * w * u[pp];
+                dG[pp][q] += 0.5f * w * u[qq];
+              }
+            }
+          }
+        }
+        float* dg = dGe + e * 9 * (int64_t)Kd + k0;
+#pragma unroll
+        for (int c = 0; c < 9; c++)
+          *reinterpret_cast<float4*>(dg + c * Kd) = make_float4(dG[c][0], dG[c][1], dG[c][2], dG[c][3]);
+      }
+#pragma unroll
+      for (int b = 0; b < BB; b += 4)
+        *reinterpret_cast<float4*>(dphi + e * BB + b) = make_float4(dp[b], dp[b + 1], dp[b + 2], dp[b + 3]);
+      float dx, dy, dz;
+      unit_bwd(u[0], u[1], u[2], r, du[0], du[1], du[2], dx, dy, dz);
+      if (acc) {
+        dvec[e * 3] += dx;
+        dvec[e * 3 + 1] += dy;
+        dvec[e * 3 + 2] += dz;
+      } else {
+        dvec[e * 3] = dx;
+        dvec[e * 3 + 1] = dy;
+        dvec[e * 3 + 2] = dz;
+      }
+    }
+  }
+}
+
 // dGt[c, a, kd] = sum_{e in row a} dGe[rev e, c, kd]   (per-edge scratch (E, 9, Kd) -> planes (9, N, Kd))
 template <typename T>
 __global__ void gather_rev_k(const T* __restrict__ src, const int32_t* __restrict__ row_ptr,
@@ -752,7 +890,13 @@ int transport_bwd(const void* phi, const void* vec, const int32_t* ej, const voi
                   smem);
   const int threads = KQ * 32 <= 256 ? KQ * 32 : 256;   // 32 edge slots per pass
   if (E > 0) {
-    if (B <= 16) {
+    if (std::is_same<T, float>::value && B == 16 && Kd % 4 == 0 && 18 * 16 * Kd * 4 <= 48 * 1024) {
+      // flagship shape: lane-per-edge kernel over the row's gradient rows in shared memory
+      const size_t smem1 = sizeof(float) * 18 * 16 * (size_t)Kd;
+      transport_bwd_lane_k<16><<<grid_for(N, 8), 64, smem1, as_stream(stream)>>>(
+          (const float*)phi, (const float*)vec, ej, (const float*)Gt, (const float*)dT1, (const float*)dT2, row_ptr,
+          (float*)dphi, (float*)dvec, acc, (float*)dGe, N, Kd);
+    } else if (B <= 16) {
       if (smem > 48 * 1024)
         cudaFuncSetAttribute(transport_bwd_k<T, 16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
       transport_bwd_k<T, 16><<<grid_for(N, 2), threads, smem, as_stream(stream)>>>(

@@ -274,6 +274,32 @@ def test_transport_fp64(small_graph):
         assert rel(u_, v_) < 1e-12
 
 
+def test_transport_fp32_matches_fp64(small_graph):
+    """fp32 transport (the lane-per-edge backward for B = 16) against the same op in float64 on the same inputs."""
+    from face_b200.ops import EdgeVec, Transport
+    g = small_graph
+    E = g["ei"].numel()
+    N = g["pos"].shape[0]
+    B, Kd = 16, 16
+    torch.manual_seed(9)
+    phi0 = torch.randn(E, B, device=DEV, dtype=torch.float64)
+    Gt0 = torch.randn(9, N, Kd, device=DEV, dtype=torch.float64)
+    G1, G2 = None, None
+    out = {}
+    for dt in (torch.float64, torch.float32):
+        gg = dict(g, pos=g["pos"].to(dt), shift=g["shift"].to(dt))
+        pos = gg["pos"].clone().requires_grad_(True)
+        phi = phi0.to(dt).requires_grad_(True)
+        Gt = Gt0.to(dt).requires_grad_(True)
+        T1, T2 = Transport.apply(phi, EdgeVec.apply(pos, gg), Gt, gg)
+        if G1 is None:
+            G1, G2 = torch.randn_like(T1), torch.randn_like(T2)
+        grads = torch.autograd.grad((T1 * G1.to(dt)).sum() + (T2 * G2.to(dt)).sum(), (pos, phi, Gt))
+        out[dt] = [T1, T2] + list(grads)
+    for a, b in zip(out[torch.float32], out[torch.float64]):
+        assert rel(a.detach().double(), b.detach()) < 2e-5
+
+
 def test_coulomb_real_fp64(small_graph):
     from face_b200.ops import CoulombReal, EdgeVec
     g = small_graph
