@@ -19,7 +19,8 @@
 //                      mbarriers.
 //   warps 0-7          split: lo = tf32(x - trunc(x)) into one of three lo planes (same swizzle), arrive; the
 //                      partial of the chunk two behind is loaded from TMEM while the split runs and folded into
-//                      fp32 registers; finished tiles are stored.  No block-wide barrier per chunk.
+//                      fp32 registers; a finished tile leaves through padded shared memory as coalesced
+//                      16-byte stores (bias and accumulate applied there).  No block-wide barrier per chunk.
 // The tensor core accumulates in fp32 with truncation, so a long chain of MMAs into one accumulator drifts toward
 // zero; each K chunk therefore starts a fresh TMEM partial (three rotate) and the partials are summed in
 // registers with round-to-nearest (the truncating chain is 12 MMAs long whatever K is).
@@ -59,9 +60,11 @@ struct GemmArgs {
 // memory of sm_100.
 template <int H16>
 struct Ring {
-  static constexpr int SA = H16 == 1 ? 9 : H16 <= 3 ? 7 : 6;
+  static constexpr int SA = H16 == 1 ? 7 : H16 <= 3 ? 5 : 4;
   static constexpr int SW = H16 == 1 ? 3 : H16 == 2 ? 3 : 2;
 };
+constexpr int kStgRow = 36;                   // epilogue staging row stride (floats): conflict-free both ways
+constexpr uint32_t kStg = kM * kStgRow * 4;   // per warpgroup (18 KB): a 128 x 32 column block
 constexpr int kLag = 2;                       // a chunk's TMEM partial is folded kLag iterations after its MMAs
 constexpr int kNB = kLag + 1;                 // TMEM partials and lo planes in rotation
 
@@ -128,7 +131,8 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUt
   unsigned char* aring = sm;                                   // SA x A tile (swizzled; = hi operand)
   unsigned char* lo_planes = aring + SA * kPlane;              // kNB x A lo (same swizzle)
   unsigned char* wring = lo_planes + kNB * kPlane;             // SW x [W hi | W lo]
-  uint64_t* fullA = reinterpret_cast<uint64_t*>(wring + SW * wbytes);
+  float* stage_out = reinterpret_cast<float*>(wring + SW * wbytes);   // 2 x epilogue staging
+  uint64_t* fullA = reinterpret_cast<uint64_t*>(wring + SW * wbytes + 2 * kStg);
   uint64_t* emptyA = fullA + SA;
   uint64_t* fullW = emptyA + SA;
   uint64_t* emptyW = fullW + SW;
@@ -246,28 +250,42 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUt
       for (int q = 0; q < HALF; q++) acc[q] += part[q];
       fence_before_sync();
       if (dc.kc == g.k_chunks - 1) {
-        const int64_t grow = dc.mt * kM + row;
-        const int64_t gc0 = (int64_t)dc.nt * Nt + wg * HALF;
-        if (grow < g.M) {
-          float* out = g.C + grow * g.ldc + gc0;
+        // tile store: the warpgroup's HALF columns in blocks of up to 32 go through padded shared memory and
+        // leave as coalesced 16-byte stores (8 lanes cover 128 contiguous bytes of one row)
+        const int64_t row0 = dc.mt * kM;
+        const int64_t gcb = (int64_t)dc.nt * Nt + wg * HALF;
+        float* stg = stage_out + wg * (kStg / 4);
 #pragma unroll
-          for (int q = 0; q < HALF; q += 4) {
-            if (gc0 + q < g.N) {
-              float4 o = make_float4(acc[q], acc[q + 1], acc[q + 2], acc[q + 3]);
+        for (int cb = 0; cb < HALF; cb += 32) {
+          const int w = HALF - cb < 32 ? HALF - cb : 32;        // 16 or 32
+          bar_sync(1 + wg, kM);                                  // staging free
+#pragma unroll
+          for (int q = 0; q < 32; q += 4)
+            if (q < w)
+              *reinterpret_cast<float4*>(stg + row * kStgRow + q) =
+                  make_float4(acc[cb + q], acc[cb + q + 1], acc[cb + q + 2], acc[cb + q + 3]);
+          bar_sync(1 + wg, kM);
+          const int cq = w / 4;                                  // float4 chunks per row
+          for (int idx = row; idx < kM * cq; idx += kM) {
+            const int r = idx / cq, c = idx - r * cq;
+            const int64_t grow = row0 + r, gc = gcb + cb + 4 * c;
+            if (grow < g.M && gc < g.N) {
+              float4 o = *reinterpret_cast<const float4*>(stg + r * kStgRow + 4 * c);
               if (g.bias) {
-                o.x += g.bias[gc0 + q];
-                o.y += g.bias[gc0 + q + 1];
-                o.z += g.bias[gc0 + q + 2];
-                o.w += g.bias[gc0 + q + 3];
+                o.x += g.bias[gc];
+                o.y += g.bias[gc + 1];
+                o.z += g.bias[gc + 2];
+                o.w += g.bias[gc + 3];
               }
+              float* out = g.C + grow * g.ldc + gc;
               if (g.beta) {
-                const float4 p = *reinterpret_cast<const float4*>(out + q);
+                const float4 p = *reinterpret_cast<const float4*>(out);
                 o.x += p.x;
                 o.y += p.y;
                 o.z += p.z;
                 o.w += p.w;
               }
-              *reinterpret_cast<float4*>(out + q) = o;
+              *reinterpret_cast<float4*>(out) = o;
             }
           }
         }
@@ -361,7 +379,8 @@ template <int H16>
 int launch_gemm(const CUtensorMap& amap, const GemmArgs& g, void* stream) {
   constexpr int Nt = 32 * H16;
   constexpr int SA = Ring<H16>::SA, SW = Ring<H16>::SW;
-  const size_t smem = (SA + kNB) * kPlane + SW * (2u * Nt * kKc * 4) + (2 * SA + 2 * SW + 2 * kNB) * 8 + 16 + 1024;
+  const size_t smem =
+      (SA + kNB) * kPlane + SW * (2u * Nt * kKc * 4) + 2 * kStg + (2 * SA + 2 * SW + 2 * kNB) * 8 + 16 + 1024;
   FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_gemm_tc: %zu B of shared memory needed", smem);
   cudaFuncSetAttribute(gemm_tc_k<H16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t units = ((g.M + kM - 1) / kM) * g.n_tiles;
