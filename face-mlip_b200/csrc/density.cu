@@ -303,21 +303,22 @@ int launch_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*>
   return launch_status("facek_density_bwd");
 }
 
-// Backward, one lane per edge (fp32, B = 16, K = 32).  A 64-thread CTA takes one row (atom) at a time: it stages
-// the row's G (20 x 512 fp32, 40 KB) in shared memory with cp.async, then each lane walks the 320 rows (x, b) of
-// G for its edge with 128-byte broadcast reads (all lanes read the same address):
-//   t = sum_k msg[k] g[k]  ->  dphi[b] += t Y[x],  dY[x] += t phi[b],   dmsg[k] += Y[x] phi[b] g[k]
-// (2 K + 3 FMAs per 8 shared vector loads), msg and dmsg of the edge in registers.  Five CTAs share an SM, so
-// one CTA's staging overlaps the others' arithmetic.  Rows with more than 64 edges loop over lane blocks.
+// Backward, two lanes per edge (fp32, B = 16, K = 32).  A 96-thread CTA takes one row (atom) at a time: it stages
+// the row's G (20 x 512 fp32, 40 KB) in shared memory with cp.async, then each lane pair walks the 320 rows (x, b)
+// of G for its edge, each lane reading its half of the row's k range as 16-byte broadcasts:
+//   t = sum_k msg[k] g[k] (one shuffle joins the halves)  ->  dphi[b] += t Y[x],  dY[x] += t phi[b]
+//   dmsg[k] += Y[x] phi[b] g[k]
+// msg and dmsg halves of the edge in registers.  96 lanes = 48 edges per round, which keeps ~90% of the lanes
+// busy at the alloys' ~44 neighbours; five CTAs share an SM, so one CTA's staging overlaps the others' work.
 template <int BB, int KK>
-__global__ void __launch_bounds__(64, 5) dens_bwd_lane_k(const float* __restrict__ phi, const float* __restrict__ msg,
+__global__ void __launch_bounds__(96, 5) dens_bwd_lane_k(const float* __restrict__ phi, const float* __restrict__ msg,
                                                          const float* __restrict__ Y, Planes<const float*> G,
                                                          float* __restrict__ dphi, float* __restrict__ dmsg,
                                                          float* __restrict__ dY, int64_t N, Rows rows) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sG = reinterpret_cast<float*>(smem_raw);              // [x][b][k]
-  constexpr int BK = BB * KK;
-  const int tid = threadIdx.x;
+  constexpr int BK = BB * KK, KH = KK / 2;
+  const int tid = threadIdx.x, half = tid & 1, slot = tid >> 1;
   for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
     int64_t e0;
     int deg;
@@ -325,17 +326,18 @@ __global__ void __launch_bounds__(64, 5) dens_bwd_lane_k(const float* __restrict
     if (deg == 0) continue;
     __syncthreads();                                           // previous row's readers are done with sG
 #pragma unroll 4
-    for (int x = 0; x < NX; x++) stage(sG + x * BK, G.at(i, x), BK, tid, 64);
+    for (int x = 0; x < NX; x++) stage(sG + x * BK, G.at(i, x), BK, tid, 96);
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    for (int t0 = 0; t0 < deg; t0 += 64) {
-      if (t0 + tid >= deg) break;
-      const int64_t e = e0 + t0 + tid;
-      float m[KK], dm[KK], p[BB], dp[BB];
+    for (int t0 = 0; t0 < deg; t0 += 48) {
+      // both lanes of a pair take the same branch (the pair shares its edge), so the shuffles below see full pairs
+      if (t0 + slot >= deg) break;
+      const int64_t e = e0 + t0 + slot;
+      float m[KH], dm[KH], p[BB], dp[BB];
 #pragma unroll
-      for (int k = 0; k < KK; k += 4) {
-        const float4 v = __ldg(reinterpret_cast<const float4*>(msg + e * KK + k));
+      for (int k = 0; k < KH; k += 4) {
+        const float4 v = __ldg(reinterpret_cast<const float4*>(msg + e * KK + half * KH + k));
         m[k] = v.x;
         m[k + 1] = v.y;
         m[k + 2] = v.z;
@@ -351,45 +353,47 @@ __global__ void __launch_bounds__(64, 5) dens_bwd_lane_k(const float* __restrict
         p[b + 3] = v.w;
         dp[b] = dp[b + 1] = dp[b + 2] = dp[b + 3] = 0.f;
       }
+      const unsigned pair_mask = __activemask();
 #pragma unroll 1
       for (int x = 0; x < NX; x++) {
         const float yx = __ldg(Y + e * NX + x);
-        const float* gx = sG + x * BK;
+        const float* gx = sG + x * BK + half * KH;
         float dyx = 0.f;
 #pragma unroll
         for (int b = 0; b < BB; b++) {
-          float g[KK];
+          float g[KH];
 #pragma unroll
-          for (int k = 0; k < KK; k += 4) {
+          for (int k = 0; k < KH; k += 4) {
             const float4 v = *reinterpret_cast<const float4*>(gx + b * KK + k);
             g[k] = v.x;
             g[k + 1] = v.y;
             g[k + 2] = v.z;
             g[k + 3] = v.w;
           }
-          float t0_ = 0.f, t1 = 0.f, t2 = 0.f, t3 = 0.f;
+          float t0_ = 0.f, t1 = 0.f;
 #pragma unroll
-          for (int k = 0; k < KK; k += 4) {
+          for (int k = 0; k < KH; k += 2) {
             t0_ += m[k] * g[k];
             t1 += m[k + 1] * g[k + 1];
-            t2 += m[k + 2] * g[k + 2];
-            t3 += m[k + 3] * g[k + 3];
           }
-          const float t = (t0_ + t1) + (t2 + t3);
+          float t = t0_ + t1;
+          t += __shfl_xor_sync(pair_mask, t, 1);
           dp[b] += t * yx;
           dyx += t * p[b];
           const float w = yx * p[b];
 #pragma unroll
-          for (int k = 0; k < KK; k++) dm[k] += w * g[k];
+          for (int k = 0; k < KH; k++) dm[k] += w * g[k];
         }
-        dY[e * NX + x] = dyx;
+        if (half == 0) dY[e * NX + x] = dyx;
+      }
+      if (half == 0) {
+#pragma unroll
+        for (int b = 0; b < BB; b += 4)
+          *reinterpret_cast<float4*>(dphi + e * BB + b) = make_float4(dp[b], dp[b + 1], dp[b + 2], dp[b + 3]);
       }
 #pragma unroll
-      for (int b = 0; b < BB; b += 4)
-        *reinterpret_cast<float4*>(dphi + e * BB + b) = make_float4(dp[b], dp[b + 1], dp[b + 2], dp[b + 3]);
-#pragma unroll
-      for (int k = 0; k < KK; k += 4)
-        *reinterpret_cast<float4*>(dmsg + e * KK + k) = make_float4(dm[k], dm[k + 1], dm[k + 2], dm[k + 3]);
+      for (int k = 0; k < KH; k += 4)
+        *reinterpret_cast<float4*>(dmsg + e * KK + half * KH + k) = make_float4(dm[k], dm[k + 1], dm[k + 2], dm[k + 3]);
     }
   }
 }
@@ -404,7 +408,7 @@ int density_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*
     if (B == 16 && K == 32) {                          // flagship shape: lane-per-edge kernel, G in shared memory
       const size_t smem = sizeof(float) * NX * 16 * 32;
       cudaFuncSetAttribute(dens_bwd_lane_k<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      dens_bwd_lane_k<16, 32><<<grid_for(N, 5), 64, smem, as_stream(stream)>>>(
+      dens_bwd_lane_k<16, 32><<<grid_for(N, 5), 96, smem, as_stream(stream)>>>(
           (const float*)phi, (const float*)msg, (const float*)Y, G, (float*)dphi, (float*)dmsg, (float*)dY, N, rows);
       return launch_status("facek_density_bwd");
     }

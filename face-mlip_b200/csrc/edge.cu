@@ -594,14 +594,15 @@ __global__ void __launch_bounds__(256) transport_bwd_k(const T* __restrict__ phi
   }
 }
 
-// Transport backward, one lane per edge (fp32, B = BB, Kd a multiple of 4).  A 64-thread CTA takes one row (atom)
-// at a time and stages its 18 gradient rows dT[o, i] (BB x Kd each) in shared memory.  For each group of 4 kd
-// channels a lane keeps g = Gt[:, j, kd..kd+3] (9 x 4), walks the 18 outputs o and for each the BB rows
-// dT[o, i, b, kd..kd+3] (16-byte broadcast reads):
+// Transport backward, two lanes per edge (fp32, B = BB, Kd a multiple of 8).  A 96-thread CTA takes one row (atom)
+// at a time and stages its 18 gradient rows dT[o, i] (BB x Kd each) in shared memory.  Each lane of an edge's pair
+// takes half of the kd channels; for each group of 4 it keeps g = Gt[:, j, kd..kd+3] (9 x 4), walks the 18
+// outputs o and for each the BB rows dT[o, i, b, kd..kd+3] (16-byte broadcast reads):
 //   dphi[b] += dT . f_o,   P_o = sum_b phi[b] dT   ->   folded at once into dV, dM (per kd) and du
-// Same outputs as transport_bwd_k.  Rows with more than 64 edges loop over lane blocks.
+// and the pair adds its dphi and du halves with shuffles.  Same outputs as transport_bwd_k.  96 lanes = 48 edges
+// per round (rows with more edges loop).
 template <int BB>
-__global__ void __launch_bounds__(64, 8) transport_bwd_lane_k(const float* __restrict__ phi,
+__global__ void __launch_bounds__(96, 5) transport_bwd_lane_k(const float* __restrict__ phi,
                                                               const float* __restrict__ vec,
                                                               const int32_t* __restrict__ ej,
                                                               const float* __restrict__ Gt,
@@ -612,7 +613,7 @@ __global__ void __launch_bounds__(64, 8) transport_bwd_lane_k(const float* __res
                                                               int acc, float* __restrict__ dGe, int64_t N, int Kd) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sD = reinterpret_cast<float*>(smem_raw);              // [o][b][kd], o in output order
-  const int tid = threadIdx.x;
+  const int tid = threadIdx.x, half = tid & 1, slot = tid >> 1;
   const int BKd = BB * Kd;
   for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
     const int64_t e0 = row_ptr[i];
@@ -622,14 +623,14 @@ __global__ void __launch_bounds__(64, 8) transport_bwd_lane_k(const float* __res
 #pragma unroll 2
     for (int o = 0; o < 18; o++) {
       const int64_t off = plane_off(trow(o), i, N, BKd);
-      stage(sD + o * BKd, trow(o) < 6 ? dT1 + off : dT2 + (off - 6 * N * (int64_t)BKd), BKd, tid, 64);
+      stage(sD + o * BKd, trow(o) < 6 ? dT1 + off : dT2 + (off - 6 * N * (int64_t)BKd), BKd, tid, 96);
     }
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
-    for (int t0 = 0; t0 < deg; t0 += 64) {
-      if (t0 + tid >= deg) break;
-      const int64_t e = e0 + t0 + tid, j = ej[e];
+    for (int t0 = 0; t0 < deg; t0 += 48) {
+      if (t0 + slot >= deg) break;                             // pairs take this branch together
+      const int64_t e = e0 + t0 + slot, j = ej[e];
       const float vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
       const float r = sqrtf(vx * vx + vy * vy + vz * vz);
       const float u[3] = {vx / r, vy / r, vz / r};
@@ -644,8 +645,9 @@ __global__ void __launch_bounds__(64, 8) transport_bwd_lane_k(const float* __res
         dp[b] = dp[b + 1] = dp[b + 2] = dp[b + 3] = 0.f;
       }
       float du[3] = {0.f, 0.f, 0.f};
+      const int kh = Kd / 2;
 #pragma unroll 1
-      for (int k0 = 0; k0 < Kd; k0 += 4) {
+      for (int k0 = half * kh; k0 < half * kh + kh; k0 += 4) {
         float g[9][4], dG[9][4];
 #pragma unroll
         for (int c = 0; c < 9; c++) {
@@ -714,6 +716,12 @@ __global__ void __launch_bounds__(64, 8) transport_bwd_lane_k(const float* __res
         for (int c = 0; c < 9; c++)
           *reinterpret_cast<float4*>(dg + c * Kd) = make_float4(dG[c][0], dG[c][1], dG[c][2], dG[c][3]);
       }
+      const unsigned pm = __activemask();
+#pragma unroll
+      for (int b = 0; b < BB; b++) dp[b] += __shfl_xor_sync(pm, dp[b], 1);
+#pragma unroll
+      for (int d = 0; d < 3; d++) du[d] += __shfl_xor_sync(pm, du[d], 1);
+      if (half) continue;
 #pragma unroll
       for (int b = 0; b < BB; b += 4)
         *reinterpret_cast<float4*>(dphi + e * BB + b) = make_float4(dp[b], dp[b + 1], dp[b + 2], dp[b + 3]);
@@ -890,10 +898,10 @@ int transport_bwd(const void* phi, const void* vec, const int32_t* ej, const voi
                   smem);
   const int threads = KQ * 32 <= 256 ? KQ * 32 : 256;   // 32 edge slots per pass
   if (E > 0) {
-    if (std::is_same<T, float>::value && B == 16 && Kd % 4 == 0 && 18 * 16 * Kd * 4 <= 48 * 1024) {
+    if (std::is_same<T, float>::value && B == 16 && Kd % 8 == 0 && 18 * 16 * Kd * 4 <= 48 * 1024) {
       // flagship shape: lane-per-edge kernel over the row's gradient rows in shared memory
       const size_t smem1 = sizeof(float) * 18 * 16 * (size_t)Kd;
-      transport_bwd_lane_k<16><<<grid_for(N, 8), 64, smem1, as_stream(stream)>>>(
+      transport_bwd_lane_k<16><<<grid_for(N, 5), 96, smem1, as_stream(stream)>>>(
           (const float*)phi, (const float*)vec, ej, (const float*)Gt, (const float*)dT1, (const float*)dT2, row_ptr,
           (float*)dphi, (float*)dvec, acc, (float*)dGe, N, Kd);
     } else if (B <= 16) {
