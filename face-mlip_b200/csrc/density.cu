@@ -303,22 +303,22 @@ int launch_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*>
   return launch_status("facek_density_bwd");
 }
 
-// Backward, two lanes per edge (fp32, B = 16, K = 32).  A 96-thread CTA takes one row (atom) at a time: it stages
-// the row's G (20 x 512 fp32, 40 KB) in shared memory with cp.async, then each lane pair walks the 320 rows (x, b)
-// of G for its edge, each lane reading its half of the row's k range as 16-byte broadcasts:
-//   t = sum_k msg[k] g[k] (one shuffle joins the halves)  ->  dphi[b] += t Y[x],  dY[x] += t phi[b]
+// Backward, L lanes per edge (fp32, B = 16, K = 32).  A 48 L-thread CTA takes one row (atom) at a time: it stages
+// the row's G (20 x 512 fp32, 40 KB) in shared memory with cp.async, then each edge's L lanes walk the 320 rows
+// (x, b) of G, each lane reading its 1/L of the row's k range as 16-byte broadcasts:
+//   t = sum_k msg[k] g[k] (shuffles join the parts)  ->  dphi[b] += t Y[x],  dY[x] += t phi[b]
 //   dmsg[k] += Y[x] phi[b] g[k]
-// msg and dmsg halves of the edge in registers.  96 lanes = 48 edges per round, which keeps ~90% of the lanes
-// busy at the alloys' ~44 neighbours; five CTAs share an SM, so one CTA's staging overlaps the others' work.
-template <int BB, int KK>
-__global__ void __launch_bounds__(96, 5) dens_bwd_lane_k(const float* __restrict__ phi, const float* __restrict__ msg,
+// msg and dmsg parts of the edge in registers.  48 edges per round keeps ~90% of the lanes busy at the alloys'
+// ~44 neighbours; five CTAs share an SM, so one CTA's staging overlaps the others' work.
+template <int BB, int KK, int L>
+__global__ void __launch_bounds__(48 * L, L >= 4 ? 4 : 5) dens_bwd_lane_k(const float* __restrict__ phi, const float* __restrict__ msg,
                                                          const float* __restrict__ Y, Planes<const float*> G,
                                                          float* __restrict__ dphi, float* __restrict__ dmsg,
                                                          float* __restrict__ dY, int64_t N, Rows rows) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sG = reinterpret_cast<float*>(smem_raw);              // [x][b][k]
-  constexpr int BK = BB * KK, KH = KK / 2;
-  const int tid = threadIdx.x, half = tid & 1, slot = tid >> 1;
+  constexpr int BK = BB * KK, KH = KK / L;
+  const int tid = threadIdx.x, half = tid % L, slot = tid / L;
   for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
     int64_t e0;
     int deg;
@@ -326,12 +326,12 @@ __global__ void __launch_bounds__(96, 5) dens_bwd_lane_k(const float* __restrict
     if (deg == 0) continue;
     __syncthreads();                                           // previous row's readers are done with sG
 #pragma unroll 4
-    for (int x = 0; x < NX; x++) stage(sG + x * BK, G.at(i, x), BK, tid, 96);
+    for (int x = 0; x < NX; x++) stage(sG + x * BK, G.at(i, x), BK, tid, 48 * L);
     cp_async_commit();
     cp_async_wait<0>();
     __syncthreads();
     for (int t0 = 0; t0 < deg; t0 += 48) {
-      // both lanes of a pair take the same branch (the pair shares its edge), so the shuffles below see full pairs
+      // the L lanes of an edge take the same branch, so the shuffles below see complete lane groups
       if (t0 + slot >= deg) break;
       const int64_t e = e0 + t0 + slot;
       float m[KH], dm[KH], p[BB], dp[BB];
@@ -377,7 +377,8 @@ __global__ void __launch_bounds__(96, 5) dens_bwd_lane_k(const float* __restrict
             t1 += m[k + 1] * g[k + 1];
           }
           float t = t0_ + t1;
-          t += __shfl_xor_sync(pair_mask, t, 1);
+#pragma unroll
+          for (int o = 1; o < L; o <<= 1) t += __shfl_xor_sync(pair_mask, t, o);
           dp[b] += t * yx;
           dyx += t * p[b];
           const float w = yx * p[b];
@@ -407,8 +408,8 @@ int density_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*
   if constexpr (sizeof(T) == 4) {
     if (B == 16 && K == 32) {                          // flagship shape: lane-per-edge kernel, G in shared memory
       const size_t smem = sizeof(float) * NX * 16 * 32;
-      cudaFuncSetAttribute(dens_bwd_lane_k<16, 32>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      dens_bwd_lane_k<16, 32><<<grid_for(N, 5), 96, smem, as_stream(stream)>>>(
+      cudaFuncSetAttribute(dens_bwd_lane_k<16, 32, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      dens_bwd_lane_k<16, 32, 2><<<grid_for(N, 5), 48 * 2, smem, as_stream(stream)>>>(
           (const float*)phi, (const float*)msg, (const float*)Y, G, (float*)dphi, (float*)dmsg, (float*)dY, N, rows);
       return launch_status("facek_density_bwd");
     }
