@@ -21,6 +21,9 @@ bool radial_tc_supported(int n_el, int nb, int H, int B);
 int radial_tc_fwd(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
                   int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2,
                   const void* b2, const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream);
+// message part of dY accumulated into dY (edge.cu)
+int edge_msg_dy(int dtype, const int32_t* ei, const int32_t* ej, const void* TJ, const void* TI, const void* dmsg,
+                int nc, int K, int64_t N, int64_t E, void* dY, void* stream);
 // bounded-wait status word of the tensor-core GEMM unit (gemm_tc.cu); -1 when it cannot be read
 int gemm_tc_status(int clear);
 

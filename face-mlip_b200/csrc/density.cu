@@ -310,11 +310,14 @@ int launch_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*>
 //   dmsg[k] += Y[x] phi[b] g[k]
 // msg and dmsg parts of the edge in registers.  48 edges per round keeps ~90% of the lanes busy at the alloys'
 // ~44 neighbours; five CTAs share an SM, so one CTA's staging overlaps the others' work.
-template <int BB, int KK, int L>
-__global__ void __launch_bounds__(48 * L, L >= 4 ? 4 : 5) dens_bwd_lane_k(const float* __restrict__ phi, const float* __restrict__ msg,
-                                                         const float* __restrict__ Y, Planes<const float*> G,
-                                                         float* __restrict__ dphi, float* __restrict__ dmsg,
-                                                         float* __restrict__ dY, int64_t N, Rows rows) {
+// With MSG, the lanes also add the message part of dY: msg[e,k] = sum_{c<nc} Y[e,c] (TJ[c,ej,k] + TI[c,ei,k]), so
+// dY[e,c] += sum_k dmsg[e,k] (TJ[c,ej,k] + TI[c,ei,k]) while dmsg is still in registers (TI may be null).
+template <int BB, int KK, int L, bool MSG>
+__global__ void __launch_bounds__(48 * L, L >= 4 ? 4 : 5)
+    dens_bwd_lane_k(const float* __restrict__ phi, const float* __restrict__ msg, const float* __restrict__ Y,
+                    Planes<const float*> G, float* __restrict__ dphi, float* __restrict__ dmsg, float* __restrict__ dY,
+                    int64_t N, Rows rows, const float* __restrict__ TJ, const float* __restrict__ TI,
+                    const int32_t* __restrict__ ej, int nc) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sG = reinterpret_cast<float*>(smem_raw);              // [x][b][k]
   constexpr int BK = BB * KK, KH = KK / L;
@@ -395,6 +398,30 @@ __global__ void __launch_bounds__(48 * L, L >= 4 ? 4 : 5) dens_bwd_lane_k(const 
 #pragma unroll
       for (int k = 0; k < KH; k += 4)
         *reinterpret_cast<float4*>(dmsg + e * KK + half * KH + k) = make_float4(dm[k], dm[k + 1], dm[k + 2], dm[k + 3]);
+      if (MSG) {
+        const int64_t NKs = N * KK;
+        const float* tjb = TJ + (int64_t)ej[e] * KK + half * KH;
+        const float* tib = TI ? TI + i * KK + half * KH : nullptr;
+#pragma unroll 1
+        for (int c = 0; c < nc; c++) {
+          float sc = 0.f;
+#pragma unroll
+          for (int k = 0; k < KH; k += 4) {
+            float4 a = __ldg(reinterpret_cast<const float4*>(tjb + c * NKs + k));
+            if (tib) {
+              const float4 t = __ldg(reinterpret_cast<const float4*>(tib + c * NKs + k));
+              a.x += t.x;
+              a.y += t.y;
+              a.z += t.z;
+              a.w += t.w;
+            }
+            sc += (dm[k] * a.x + dm[k + 1] * a.y) + (dm[k + 2] * a.z + dm[k + 3] * a.w);
+          }
+#pragma unroll
+          for (int o = 1; o < L; o <<= 1) sc += __shfl_xor_sync(pair_mask, sc, o);
+          if (half == 0) dY[e * NX + c] += sc;
+        }
+      }
     }
   }
 }
@@ -408,9 +435,10 @@ int density_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*
   if constexpr (sizeof(T) == 4) {
     if (B == 16 && K == 32) {                          // flagship shape: lane-per-edge kernel, G in shared memory
       const size_t smem = sizeof(float) * NX * 16 * 32;
-      cudaFuncSetAttribute(dens_bwd_lane_k<16, 32, 2>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
-      dens_bwd_lane_k<16, 32, 2><<<grid_for(N, 5), 48 * 2, smem, as_stream(stream)>>>(
-          (const float*)phi, (const float*)msg, (const float*)Y, G, (float*)dphi, (float*)dmsg, (float*)dY, N, rows);
+      cudaFuncSetAttribute(dens_bwd_lane_k<16, 32, 2, false>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+      dens_bwd_lane_k<16, 32, 2, false><<<grid_for(N, 5), 48 * 2, smem, as_stream(stream)>>>(
+          (const float*)phi, (const float*)msg, (const float*)Y, G, (float*)dphi, (float*)dmsg, (float*)dY, N, rows,
+          nullptr, nullptr, nullptr, 0);
       return launch_status("facek_density_bwd");
     }
     if (B <= 16) return launch_bwd<T, 8, 16>(phi, msg, Y, G, dphi, dmsg, dY, N, rows, B, K, stream);
@@ -459,10 +487,46 @@ int xm_bwd(const void* phi, const void* msg, const void* Y, const void* G0, cons
   return density_bwd<T>(phi, msg, Y, P, dphi, dmsg, dY, N, 0, B, K, row_ptr, stream);
 }
 
+// density adjoint plus the message part of dY (xm layout, CSR rows): the lane kernel does both for fp32 B=16 K=32;
+// other shapes run the density adjoint and then the message dY kernel accumulating into dY
+template <typename T>
+int xm_msg_bwd(const void* phi, const void* msg, const void* Y, const void* G0, const void* G1, const void* G2,
+               const void* G3, const void* TJ, const void* TI, const int32_t* ei, const int32_t* ej, int nc,
+               void* dphi, void* dmsg, void* dY, int64_t N, int64_t E, int B, int K, const int32_t* row_ptr,
+               void* stream) {
+  if (std::is_same<T, float>::value && B == 16 && K == 32) {
+    const int64_t pl = N * (int64_t)B * K;
+    Planes<const float*> P{{(const float*)G0, (const float*)G1, (const float*)G2, (const float*)G3}, (int64_t)B * K,
+                           pl};
+    const size_t smem = sizeof(float) * NX * 16 * 32;
+    cudaFuncSetAttribute(dens_bwd_lane_k<16, 32, 2, true>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+    dens_bwd_lane_k<16, 32, 2, true><<<grid_for(N, 5), 48 * 2, smem, as_stream(stream)>>>(
+        (const float*)phi, (const float*)msg, (const float*)Y, P, (float*)dphi, (float*)dmsg, (float*)dY, N,
+        Rows{row_ptr, 0}, (const float*)TJ, (const float*)TI, ej, nc);
+    return launch_status("facek_density_msg_xm_bwd");
+  }
+  int st = xm_bwd<T>(phi, msg, Y, G0, G1, G2, G3, dphi, dmsg, dY, N, B, K, row_ptr, stream);
+  if (st) return st;
+  return edge_msg_dy(sizeof(T) == 4 ? FACEK_F32 : FACEK_F64, ei, ej, TJ, TI, dmsg, nc, K, N, E, dY, stream);
+}
+
 }  // namespace
 }  // namespace facek
 
 using namespace facek;
+
+extern "C" int facek_density_msg_xm_bwd(int dtype, const void* phi, const void* msg, const void* Y, const void* G0,
+                                        const void* G1, const void* G2, const void* G3, const void* TJ,
+                                        const void* TI, const int32_t* ei, const int32_t* ej, int32_t nc, void* dphi,
+                                        void* dmsg, void* dY, int64_t N, int64_t E, int32_t B, int32_t K,
+                                        const int32_t* row_ptr, void* stream) {
+  FACEK_CHECK_ARG(N >= 0 && E >= 0 && B > 0 && K > 0 && nc >= 1 && nc <= 10 && row_ptr && G0 && G1 && G2 && G3 &&
+                      TJ && ei && ej,
+                  "facek_density_msg_xm_bwd: bad arguments");
+  if (N == 0) return FACEK_OK;
+  return FACEK_DISPATCH(dtype, xm_msg_bwd, phi, msg, Y, G0, G1, G2, G3, TJ, TI, ei, ej, nc, dphi, dmsg, dY, N, E, B,
+                        K, row_ptr, stream);
+}
 
 extern "C" int facek_density_fwd(int dtype, const void* phi, const void* msg, const void* Y, void* D, int64_t N,
                                  int32_t M, int32_t B, int32_t K, const int32_t* row_ptr, void* stream) {

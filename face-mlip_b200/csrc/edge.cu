@@ -928,6 +928,20 @@ int transport_bwd(const void* phi, const void* vec, const int32_t* ej, const voi
 }
 
 }  // namespace
+
+// message part of dY only, accumulated into dY (used after a density adjoint that wrote dY)
+int edge_msg_dy(int dtype, const int32_t* ei, const int32_t* ej, const void* TJ, const void* TI, const void* dmsg,
+                int nc, int K, int64_t N, int64_t E, void* dY, void* stream) {
+  if (E == 0) return FACEK_OK;
+  if (dtype == FACEK_F32)
+    edge_msg_bwd_dy_k<float><<<grid_for(ceil_div<int64_t>(E, 8), 16), 256, 0, as_stream(stream)>>>(
+        ei, ej, (const float*)TJ, (const float*)TI, (const float*)dmsg, nc, K, N, (float*)dY, 1, E);
+  else
+    edge_msg_bwd_dy_k<double><<<grid_for(ceil_div<int64_t>(E, 8), 16), 256, 0, as_stream(stream)>>>(
+        ei, ej, (const double*)TJ, (const double*)TI, (const double*)dmsg, nc, K, N, (double*)dY, 1, E);
+  return launch_status("facek_density_msg_xm_bwd(message dY)");
+}
+
 }  // namespace facek
 
 using namespace facek;

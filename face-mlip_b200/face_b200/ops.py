@@ -173,6 +173,48 @@ class Density(torch.autograd.Function):
         return dphi, dmsg, dY, None
 
 
+class DensityMsg(torch.autograd.Function):
+    """Directional messages and the factorised density in one op: msg[e,k] = sum_{c<nc} Y[e,c] (TJ[c,ej,k] +
+    TI[c,ei,k]), D[x, i, b*K+k] = sum_{e in row i} phi[e,b] msg[e,k] Y[e,x] (face/model.py:473-513).  The adjoint
+    runs the density backward and the message part of dY in one kernel (facek_density_msg_xm_bwd), then the
+    message-table adjoint (facek_edge_msg_bwd without dY).  Returns the four rank blocks of D."""
+
+    @staticmethod
+    def forward(ctx, phi, Y, TJ, TI, gr):
+        E = Y.shape[0]
+        nc, N, K = TJ.shape
+        B = phi.shape[1]
+        TJ = TJ.contiguous()
+        TI = TI.contiguous() if TI is not None else None
+        msg = torch.empty(E, K, dtype=Y.dtype, device=Y.device)
+        _lib.call("facek_edge_msg_fwd", _tag(Y), _p(Y), _p(gr["ei"]), _p(gr["ej"]), _p(TJ), _p(TI), nc, K, _p(msg),
+                  N, E, _lib.stream())
+        D = torch.empty(20, N, B * K, dtype=phi.dtype, device=phi.device)
+        _lib.call("facek_density_xm_fwd", _tag(phi), _p(phi), _p(msg), _p(Y), _p(D), N, B, K, _p(gr["row_ptr"]),
+                  _lib.stream())
+        ctx.save_for_backward(phi, msg, Y, TJ, TI)
+        ctx.gr = gr
+        return tuple(D[a:b] for a, b in RANK)
+
+    @staticmethod
+    def backward(ctx, *dD):
+        phi, msg, Y, TJ, TI = ctx.saved_tensors
+        gr = ctx.gr
+        nc, N, K = TJ.shape
+        E, B = phi.shape
+        G = [g.contiguous() if g is not None else torch.zeros(b - a, N, B * K, dtype=phi.dtype, device=phi.device)
+             for g, (a, b) in zip(dD, RANK)]
+        dphi, dmsg, dY = torch.empty_like(phi), torch.empty_like(msg), torch.empty_like(Y)
+        _lib.call("facek_density_msg_xm_bwd", _tag(phi), _p(phi), _p(msg), _p(Y), *[_p(g) for g in G], _p(TJ), _p(TI),
+                  _p(gr["ei"]), _p(gr["ej"]), nc, _p(dphi), _p(dmsg), _p(dY), N, E, B, K, _p(gr["row_ptr"]),
+                  _lib.stream())
+        dTJ = torch.empty_like(TJ)
+        dTI = torch.empty_like(TI) if TI is not None else None
+        _lib.call("facek_edge_msg_bwd", _tag(Y), _p(Y), _p(gr["ei"]), _p(gr["ej"]), _p(TJ), _p(TI), _p(dmsg),
+                  _p(gr["row_ptr"]), _p(gr["rev"]), nc, K, None, 0, _p(dTJ), _p(dTI), N, E, _lib.stream())
+        return dphi, dY, dTJ, dTI, None
+
+
 class Transport(torch.autograd.Function):
     """Transport sums as two planes (3, N, 2*B*Kd) [V, M u] and (6, N, 2*B*Kd) [M, sym(u V)], Gt (9, N, Kd)."""
 
@@ -525,10 +567,9 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
         TI = torch.cat([torch.zeros_like(msgtab)[None], Vd @ w3, (Md @ w4) * q["y2w"]], 0)
         if q["transport"]:
             Gt = torch.cat([Vb[..., Kd:], Mb[..., Kd:]], 0)                           # (9, N, Kd)
-        mj = EdgeMsg.apply(Y, TJ, TI, gr)
+        D = DensityMsg.apply(phi, Y, TJ, TI, gr)                                     # 4 x (k_l, N, B*K)
     else:
-        mj = EdgeMsg.apply(Y, msgtab[None], None, gr)
-    D = Density.apply(phi, mj, Y, gr)                                                # 4 x (k_l, N, B*K)
+        D = DensityMsg.apply(phi, Y, msgtab[None], None, gr)
     s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1)   # (4, N, C)
     tpl = {}
     if Gt is not None:

@@ -46,6 +46,14 @@ int facek_density_xm_fwd(int dtype, const void* phi, const void* msg, const void
 int facek_density_xm_bwd(int dtype, const void* phi, const void* msg, const void* Y, const void* G0, const void* G1,
                          const void* G2, const void* G3, void* dphi, void* dmsg, void* dY, int64_t N, int32_t B,
                          int32_t K, const int32_t* row_ptr, void* stream);
+/* Density adjoint fused with the message part of dY (face/model.py:473-513; the reference runs the CuPy density
+ * backward, face/kernels.py:56-118, and autograd through the message GEMV): the outputs of facek_density_xm_bwd,
+ * with dY[e, c] (c < nc) additionally += sum_k dmsg[e,k] (TJ[c, ej, k] + TI[c, ei, k]), TJ/TI (nc, N, K) as in
+ * facek_edge_msg_fwd (TI may be NULL).  dTJ/dTI then come from facek_edge_msg_bwd with dY = NULL. */
+int facek_density_msg_xm_bwd(int dtype, const void* phi, const void* msg, const void* Y, const void* G0,
+                             const void* G1, const void* G2, const void* G3, const void* TJ, const void* TI,
+                             const int32_t* ei, const int32_t* ej, int32_t nc, void* dphi, void* dmsg, void* dY,
+                             int64_t N, int64_t E, int32_t B, int32_t K, const int32_t* row_ptr, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------
  * Node invariant algebra, reference layout.  Replaces face-mlip face/node_kernel.py:18-64 (node_fwd) and

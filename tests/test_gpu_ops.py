@@ -245,6 +245,30 @@ def test_density_csr_fp64(small_graph):
         assert rel(u, v) < 1e-12
 
 
+@pytest.mark.parametrize("dt,nc", [(torch.float64, 10), (torch.float32, 10), (torch.float32, 1)])
+def test_density_msg_fused_matches_composed(small_graph, dt, nc):
+    """DensityMsg (message + density with the fused adjoint) against EdgeMsg followed by Density on the same
+    inputs: D and the gradients with respect to phi, Y, TJ, TI."""
+    from face_b200.ops import Density, DensityMsg, EdgeMsg
+    g = small_graph
+    E = g["ei"].numel()
+    N = g["pos"].shape[0]
+    torch.manual_seed(11)
+    mk = lambda *s: torch.randn(*s, device=DEV, dtype=torch.float64).to(dt).requires_grad_(True)
+    phi, Y, TJ = mk(E, 16), mk(E, 20), mk(nc, N, 32)
+    TI = mk(nc, N, 32) if nc > 1 else None
+    wrt = [phi, Y, TJ] + ([TI] if TI is not None else [])
+    D1 = torch.cat(DensityMsg.apply(phi, Y, TJ, TI, g), 0)
+    D2 = torch.cat(Density.apply(phi, EdgeMsg.apply(Y, TJ, TI, g), Y, g), 0)
+    tol = 1e-12 if dt == torch.float64 else 1e-5
+    assert rel(D1.detach().double(), D2.detach().double()) < tol
+    G = torch.randn_like(D1)
+    g1 = torch.autograd.grad((D1 * G).sum(), wrt)
+    g2 = torch.autograd.grad((D2 * G).sum(), wrt)
+    for a, b in zip(g1, g2):
+        assert rel(a.double(), b.double()) < tol
+
+
 def test_transport_fp64(small_graph):
     from face_b200.ops import EdgeVec, Transport
     g = small_graph
