@@ -15,14 +15,14 @@
 //                      to their "empty" mbarriers, so the HBM stream runs SA - 1 chunks ahead of the MMAs.
 //   warp 10, lane 0    MMA issuer: once all 256 compute threads have arrived on the chunk's "split" mbarrier and
 //                      its W chunk has landed, 4 K-steps x 3 split terms of M=128 x N=Nt x K=8 MMAs into one of
-//                      three TMEM partials, then commits to the partial's, the A stage's and the W stage's
+//                      four TMEM partials, then commits to the partial's, the A stage's and the W stage's
 //                      mbarriers.
-//   warps 0-7          split: lo = tf32(x - trunc(x)) into one of three lo planes (same swizzle), arrive; the
-//                      partial of the chunk two behind is loaded from TMEM while the split runs and folded into
+//   warps 0-7          split: lo = tf32(x - trunc(x)) into one of four lo planes (same swizzle), arrive; the
+//                      partial of the chunk three behind is loaded from TMEM while the split runs and folded into
 //                      fp32 registers; a finished tile leaves through padded shared memory as coalesced
 //                      16-byte stores (bias and accumulate applied there).  No block-wide barrier per chunk.
 // The tensor core accumulates in fp32 with truncation, so a long chain of MMAs into one accumulator drifts toward
-// zero; each K chunk therefore starts a fresh TMEM partial (three rotate) and the partials are summed in
+// zero; each K chunk therefore starts a fresh TMEM partial (four rotate) and the partials are summed in
 // registers with round-to-nearest (the truncating chain is 12 MMAs long whatever K is).
 //
 // CTAs are persistent over (M tile, N tile) units (consecutive units share the A tile, so its re-reads hit L2).
@@ -60,12 +60,12 @@ struct GemmArgs {
 // memory of sm_100.
 template <int H16>
 struct Ring {
-  static constexpr int SA = H16 == 1 ? 7 : H16 <= 3 ? 5 : 4;
+  static constexpr int SA = H16 == 1 ? 6 : H16 == 2 ? 4 : H16 == 3 ? 4 : 3;
   static constexpr int SW = H16 == 1 ? 3 : H16 == 2 ? 3 : 2;
 };
 constexpr int kStgRow = 36;                   // epilogue staging row stride (floats): conflict-free both ways
 constexpr uint32_t kStg = kM * kStgRow * 4;   // per warpgroup (18 KB): a 128 x 32 column block
-constexpr int kLag = 2;                       // a chunk's TMEM partial is folded kLag iterations after its MMAs
+constexpr int kLag = 3;                       // a chunk's TMEM partial is folded kLag iterations after its MMAs
 constexpr int kNB = kLag + 1;                 // TMEM partials and lo planes in rotation
 
 // byte offset of the 16-byte quad q of row r in a 128-byte-swizzled K-major plane (1024-byte aligned)
