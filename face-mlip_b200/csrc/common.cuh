@@ -21,6 +21,10 @@ bool radial_tc_supported(int n_el, int nb, int H, int B);
 int radial_tc_fwd(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
                   int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2,
                   const void* b2, const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream);
+// tensor-core density forward, fp32 B=16 K=32, component-major planes (density_tc.cu) and its status word
+int density_tc_xm_fwd(const float* phi, const float* msg, const float* Y, float* D, int64_t N,
+                      const int32_t* row_ptr, void* stream);
+int density_tc_status(int clear);
 // message part of dY accumulated into dY (edge.cu)
 int edge_msg_dy(int dtype, const int32_t* ei, const int32_t* ej, const void* TJ, const void* TI, const void* dmsg,
                 int nc, int K, int64_t N, int64_t E, void* dY, void* stream);

@@ -336,8 +336,8 @@ extern "C" int facek_tc_status(int32_t* status, int32_t clear) {
     if (cudaMemcpyToSymbol(tc::g_tc_status, &zero, sizeof(int)) != cudaSuccess)
       return launch_status("facek_tc_status");
   }
-  const int g = gemm_tc_status(clear);
-  if (g < 0) return launch_status("facek_tc_status");
-  *status = v | g;
+  const int g = gemm_tc_status(clear), d = density_tc_status(clear);
+  if (g < 0 || d < 0) return launch_status("facek_tc_status");
+  *status = v | g | d;
   return FACEK_OK;
 }

@@ -41,6 +41,7 @@ SIGNATURES = {
     "facek_edge_sym": [I32, P, P, I64, P],
     "facek_edge_sym_bwd": [I32, P, P, P, I32, I64, P],
     "facek_radial_fwd": [I32, P, P, P, P, I32, D, I32, I32, I32, P, P, P, P, P, P, P, P, P, I64, P],
+    "facek_density_tc_xm_fwd": [P, P, P, P, I64, I32, I32, P, P],
     "facek_density_msg_xm_bwd": [I32, P, P, P, P, P, P, P, P, P, P, P, I32, P, P, P, I64, I64, I32, I32, P, P],
     "facek_radial_simt_fwd": [I32, P, P, P, P, I32, D, I32, I32, I32, P, P, P, P, P, P, P, P, P, I64, P],
     "facek_radial_tc_fwd": [P, P, P, P, I32, D, I32, I32, I32, P, P, P, P, P, P, P, P, P, I64, P],

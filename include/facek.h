@@ -46,6 +46,12 @@ int facek_density_xm_fwd(int dtype, const void* phi, const void* msg, const void
 int facek_density_xm_bwd(int dtype, const void* phi, const void* msg, const void* Y, const void* G0, const void* G1,
                          const void* G2, const void* G3, void* dphi, void* dmsg, void* dY, int64_t N, int32_t B,
                          int32_t K, const int32_t* row_ptr, void* stream);
+/* facek_density_xm_fwd on the tcgen05 tensor cores (fp32, B = 16, K = 32 only): per atom the GEMM
+ * D_i[(x,b), k] = sum_e (Y[e,x] phi[e,b]) msg[e,k] with M/N-major operands and the 3-term tf32 split.  Same
+ * outputs as facek_density_xm_fwd to fp32 accuracy; at present slower than it on the cfg5 alloy, so the default
+ * entry keeps the CUDA-core kernel.  No reference counterpart as a C entry point (face/kernels.py:22-54). */
+int facek_density_tc_xm_fwd(const float* phi, const float* msg, const float* Y, float* D, int64_t N, int32_t B,
+                            int32_t K, const int32_t* row_ptr, void* stream);
 /* Density adjoint fused with the message part of dY (face/model.py:473-513; the reference runs the CuPy density
  * backward, face/kernels.py:56-118, and autograd through the message GEMV): the outputs of facek_density_xm_bwd,
  * with dY[e, c] (c < nc) additionally += sum_k dmsg[e,k] (TJ[c, ej, k] + TI[c, ei, k]), TJ/TI (nc, N, K) as in

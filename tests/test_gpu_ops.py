@@ -356,6 +356,46 @@ def test_pme_golden_fp64():
     assert float((gq.cpu() - torch.tensor(k["recip_dq"])).abs().max()) < 1e-11
 
 
+@pytest.mark.parametrize("entry", ["facek_density_xm_fwd", "facek_density_tc_xm_fwd"])
+def test_density_xm_fwd_fp32_ragged_rows(entry):
+    """Flagship shape (B=16, K=32) in fp32 (CUDA-core default and tensor-core entry) on CSR rows of degree 0..150
+    (empty rows, ragged 8-edge steps, rows spanning three 64-edge blocks) through the C ABI, against the default
+    entry point in float64."""
+    from face_b200 import _lib
+    g = torch.Generator().manual_seed(12)
+    N = 2003
+    deg = torch.randint(0, 80, (N,), generator=g)
+    deg[::9] = 0
+    deg[5::97] = 150
+    row_ptr = torch.zeros(N + 1, dtype=torch.int32)
+    row_ptr[1:] = torch.cumsum(deg, 0).to(torch.int32)
+    E = int(row_ptr[-1])
+    row_ptr = row_ptr.to(DEV)
+    phi = torch.randn(E, 16, generator=g, dtype=torch.float64).to(DEV)
+    msg = torch.randn(E, 32, generator=g, dtype=torch.float64).to(DEV)
+    Y = torch.randn(E, 20, generator=g, dtype=torch.float64).to(DEV)
+    out = {}
+    for dt in (torch.float64, torch.float32):
+        a = [t.to(dt).contiguous() for t in (phi, msg, Y)]
+        D = torch.full((20, N, 512), float("nan"), dtype=dt, device=DEV)
+        p = _lib.ptr
+        if dt == torch.float32 and entry == "facek_density_tc_xm_fwd":
+            _lib.call(entry, *[p(t) for t in a], p(D), N, 16, 32, p(row_ptr), _lib.stream())
+        else:
+            _lib.call("facek_density_xm_fwd", _lib.dtype_tag(a[0]), *[p(t) for t in a], p(D), N, 16, 32,
+                      p(row_ptr), _lib.stream())
+        torch.cuda.synchronize()
+        out[dt] = D
+    assert torch.isfinite(out[torch.float32]).all()
+    assert rel(out[torch.float32].double(), out[torch.float64]) < 1e-5
+    empty = (deg == 0).nonzero().flatten().to(DEV)
+    assert (out[torch.float32][:, empty] == 0).all()
+    import ctypes
+    st = ctypes.c_int32(-1)
+    _lib.call("facek_tc_status", ctypes.byref(st), 1)
+    assert st.value == 0
+
+
 def test_density_xm_bwd_fp32_ragged_rows():
     """Flagship shape (B=16, K=32) in fp32 on CSR rows of degree 0..70 (empty rows included) through the C ABI,
     against the same entry point in float64."""
