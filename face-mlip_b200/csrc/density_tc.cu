@@ -8,15 +8,13 @@
 // atom, 32-byte chunks XOR-ed with (row % 4).
 // fp32 accuracy through the 3-term tf32 split (tc.cuh); the chain per tile is at most 3 x ceil(deg/8) MMAs.
 //
-// Status: exact to fp32 level (tests hold it to 1e-5 of float64) but slower than the CUDA-core kernel on the
-// cfg5 alloy (38.8 vs 32.7 ms per launch): each atom runs three serialized build -> MMA -> wait -> store rounds
-// in two 4-warp CTAs per SM, so the latencies are exposed.  facek_density_xm_fwd keeps the CUDA-core kernel;
-// this one is reachable as facek_density_tc_xm_fwd.
+// Atoms with more than 64 edges accumulate over 64-edge blocks; atoms without edges get zero rows.  The work
+// layout and warp roles are described at the kernel.
 //
-// CTA = 128 threads (two per SM): thread (e = t % 64, half = t / 64) builds half of a tile's V groups for edge
-// e; thread 0 issues the MMAs; for the epilogue thread t owns TMEM lane t, stages its 32 k values in padded
-// shared memory and the tile leaves as coalesced 2 KB x-planes.  Atoms with more than 64 edges accumulate over
-// 64-edge blocks; atoms without edges get zero rows.  Every wait is bounded (tc.cuh).
+// Status: exact to fp32 level (tests hold it to 1e-5 of float64) but not yet faster than the CUDA-core kernel on
+// the cfg5 alloy (43.4 vs 32.9 ms per launch): the eight builder warps both build operands and store finished
+// tiles, so the stores stall the build.  facek_density_xm_fwd keeps the CUDA-core kernel; this one is reachable
+// as facek_density_tc_xm_fwd.
 #include "common.cuh"
 #include "tc.cuh"
 
@@ -27,12 +25,10 @@ using namespace tc;
 
 constexpr int kNX = 20, kB = 16, kK = 32, kBK = kB * kK;
 constexpr int kEB = 64;                              // edges per K block
-constexpr int kThreads = 128;
 constexpr uint32_t kGroup = kEB * 128;               // one 32-wide MN group x 64 edge rows (8 KB)
 constexpr uint32_t kVPlane = 4 * kGroup;             // a 128-row M tile's V (hi or lo) plane, 32 KB
 constexpr uint32_t kMsgPlane = kEB * 128;            // msg block (hi or lo), 8 KB
 constexpr int kStgRow = 36;                          // epilogue staging row stride (floats)
-constexpr uint32_t kSmem = 2 * kVPlane + 2 * kMsgPlane + kThreads * kStgRow * 4 + 64 + 1024;
 
 // byte offset of 16-byte quad q (fp32 elements 4q .. 4q+3 along MN) of K-row r in a 128-byte-base-32-byte
 // swizzled MN-major plane: 32-byte chunk q/2 goes to position (q/2) ^ (r % 4)
@@ -62,28 +58,75 @@ __device__ __forceinline__ float4 split_lo4(float4 v) {
 __device__ __forceinline__ float4 split_hi4(float4 v) {
   return make_float4(to_tf32(v.x), to_tf32(v.y), to_tf32(v.z), to_tf32(v.w));
 }
+__device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(mbar)) : "memory");
+}
 
-__global__ void __launch_bounds__(kThreads, 2)
+// Pipelined version.  Work is a sequence of chunks c = (atom, tile T, 64-edge block kb), 3 x nkb per atom.
+// Warps 0-7 (builders): wait for ring stage c % 2 to be free, write the chunk's V (hi, lo) and msg (hi, lo) planes,
+// arrive on full[c % 2] (256 arrivals).  Warp 8 (MMA issuer): wait full, issue up to 8 K-steps x 3 terms into
+// TMEM accumulator (tile index) % 4, commit empty[stage] and, on a tile's last block, done[acc].  The builders
+// store tile t two tiles after issuing it (wait done, TMEM -> padded staging -> coalesced 2 KB x-planes), so the
+// MMAs of tiles t+1, t+2 overlap its store.  Every wait is bounded; parity waits are never two phases behind.
+constexpr int kPThreads = 288;                       // 8 builder warps + MMA warp
+constexpr int kAcc = 4;                              // TMEM accumulators in rotation (32 columns each)
+constexpr int kLagT = 2;                             // tiles between a tile's last chunk and its store
+constexpr uint32_t kStage = 2 * kVPlane + 2 * kMsgPlane;   // 80 KB
+constexpr uint32_t kPSmem = 2 * kStage + 2 * 64 * kStgRow * 4 + 128 + 1024;
+
+struct ChunkCursor {                                 // (atom, tile, block) sequence of one CTA
+  int64_t i, e0;
+  int deg, T, kb, nkb;
+  __device__ bool load(int64_t atom, const int32_t* row_ptr, int64_t N) {
+    i = atom;
+    if (i >= N) return false;
+    e0 = row_ptr[i];
+    deg = row_ptr[i + 1] - (int)e0;
+    T = 0;
+    kb = 0;
+    nkb = deg > 0 ? (deg + kEB - 1) / kEB : 0;
+    return true;
+  }
+  // next chunk; atoms without edges are skipped (their rows are zeroed separately)
+  __device__ bool next(const int32_t* row_ptr, int64_t N, int64_t stride) {
+    if (nkb > 0 && ++kb < nkb) return true;
+    kb = 0;
+    if (nkb > 0 && ++T < 3) return true;
+    do {
+      if (!load(i + stride, row_ptr, N)) return false;
+    } while (nkb == 0);
+    return true;
+  }
+  __device__ bool first(int64_t atom, const int32_t* row_ptr, int64_t N, int64_t stride) {
+    if (!load(atom, row_ptr, N)) return false;
+    while (nkb == 0)
+      if (!load(i + stride, row_ptr, N)) return false;
+    return true;
+  }
+};
+
+__global__ void __launch_bounds__(kPThreads, 1)
     dens_fwd_tc_k(const float* __restrict__ phi, const float* __restrict__ msg, const float* __restrict__ Y,
                   float* __restrict__ D, int64_t N, int64_t E, const int32_t* __restrict__ row_ptr) {
   extern __shared__ unsigned char sm_raw[];
   unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);
-  unsigned char* vhi = sm;
-  unsigned char* vlo = vhi + kVPlane;
-  unsigned char* mhi = vlo + kVPlane;
-  unsigned char* mlo = mhi + kMsgPlane;
-  float* stg = reinterpret_cast<float*>(mlo + kMsgPlane);
-  uint64_t* mbar = reinterpret_cast<uint64_t*>(stg + kThreads * kStgRow);
-  uint32_t* slot = reinterpret_cast<uint32_t*>(mbar + 1);
+  float* stg = reinterpret_cast<float*>(sm + 2 * kStage);     // epilogue staging: 128 rows x kStgRow floats
+  uint64_t* full = reinterpret_cast<uint64_t*>(sm + 2 * kStage + 2 * 64 * kStgRow * 4);
+  uint64_t* empty = full + 2;
+  uint64_t* done = empty + 2;                                  // [kAcc]
+  uint32_t* slot = reinterpret_cast<uint32_t*>(done + kAcc);
   int* abort_ = reinterpret_cast<int*>(slot + 1);
 
-  const int tid = threadIdx.x, warp = tid >> 5;
-  const int eb = tid & (kEB - 1), half = tid >> 6;
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
   const int64_t plane = N * (int64_t)kBK;
 
   if (tid == 0) {
     *abort_ = 0;
-    mbar_init(mbar, 1);
+    for (int s = 0; s < 2; s++) {
+      mbar_init(&full[s], 256);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < kAcc; a++) mbar_init(&done[a], 1);
     fence_mbar_init();
   }
   if (warp == 0) {
@@ -94,112 +137,179 @@ __global__ void __launch_bounds__(kThreads, 2)
   __syncthreads();
   fence_after_sync();
   const uint32_t tbase = *slot;
-  const uint32_t tl = tbase + ((uint32_t)(warp * 32) << 16);
   volatile int* ab = abort_;
-  uint32_t parity = 0;
-  const uint32_t idesc = idesc_tf32_mn(128, kK);
 
-  for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
-    const int64_t e0 = row_ptr[i];
-    const int deg = row_ptr[i + 1] - (int)e0;
-    if (deg == 0) {                                     // zero rows: 20 planes x 512 floats
-      for (int q = tid; q < kNX * kBK / 4; q += kThreads) {
-        const int x = q / (kBK / 4), c = q % (kBK / 4);
-        reinterpret_cast<float4*>(D + x * plane + i * kBK)[c] = make_float4(0.f, 0.f, 0.f, 0.f);
-      }
-      continue;
-    }
-    const int nkb = (deg + kEB - 1) / kEB;
-    for (int T = 0; T < 3; T++) {
-      const int g0 = 4 * T;                             // first 32-wide (x, b) group of this tile
-      for (int kb = 0; kb < nkb; kb++) {
-        const int nb = min(kEB, deg - kb * kEB);        // edges in this block
-        const int64_t eblk = e0 + kb * kEB;
-        __syncthreads();                                // previous MMA's operands are no longer read
-        // msg block: rows eblk .. eblk+63 (rows past the block are other atoms' edges: V is zero there)
-        if (T == 0 || nkb > 1) {
-          for (int q = tid; q < kEB * 8; q += kThreads) {
-            const int r = q >> 3, c = q & 7;
-            float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-            if (r < nb) v = __ldg(reinterpret_cast<const float4*>(msg + (eblk + r) * kK) + c);
-            *reinterpret_cast<float4*>(mhi + sw32b(r, c)) = split_hi4(v);
-            *reinterpret_cast<float4*>(mlo + sw32b(r, c)) = split_lo4(v);
-          }
-        }
-        // V groups of this tile for edge eb (two groups per thread half; zero rows past the block)
-        const bool live = eb < nb;
-        const int64_t e = eblk + eb;
-        float p[kB];
-#pragma unroll
-        for (int b = 0; b < kB; b += 4) {
-          float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
-          if (live) v = __ldg(reinterpret_cast<const float4*>(phi + e * kB + b));
-          p[b] = v.x;
-          p[b + 1] = v.y;
-          p[b + 2] = v.z;
-          p[b + 3] = v.w;
-        }
-#pragma unroll
-        for (int gs = 0; gs < 2; gs++) {
-          const int slotg = 2 * half + gs;              // group slot within the tile
-          const int g = g0 + slotg;
-          if (g >= 10) continue;                        // tile 2 holds groups 8, 9 only
-          const float y0 = live ? __ldg(Y + e * kNX + 2 * g) : 0.f;
-          const float y1 = live ? __ldg(Y + e * kNX + 2 * g + 1) : 0.f;
-          unsigned char* gh = vhi + slotg * kGroup;
-          unsigned char* gl = vlo + slotg * kGroup;
-#pragma unroll
-          for (int q = 0; q < 8; q++) {                 // 16-byte quad q: (x, b) = (2g + q/4, 4(q%4) .. +3)
-            const float y = q < 4 ? y0 : y1;
-            const int b = 4 * (q & 3);
-            const float4 v = make_float4(y * p[b], y * p[b + 1], y * p[b + 2], y * p[b + 3]);
-            *reinterpret_cast<float4*>(gh + sw32b(eb, q)) = split_hi4(v);
-            *reinterpret_cast<float4*>(gl + sw32b(eb, q)) = split_lo4(v);
-          }
-        }
-        fence_proxy_async_smem();
-        __syncthreads();
-        if (*ab) break;                                 // uniform (read after the barrier)
-        if (tid == 0) {
-          fence_after_sync();
-          const uint32_t ah = smem_u32(vhi), al = smem_u32(vlo), bh = smem_u32(mhi), bl = smem_u32(mlo);
-          const uint32_t dcol = tbase + T * kK;
-          const int nks = (nb + 7) / 8;
-          for (int s = 0; s < nks; s++) {
-            const uint64_t dah = desc_mn_sw32b(ah + s * 1024, kGroup, 512);
-            const uint64_t dal = desc_mn_sw32b(al + s * 1024, kGroup, 512);
-            const uint64_t dbh = desc_mn_sw32b(bh + s * 1024, kMsgPlane, 512);
-            const uint64_t dbl = desc_mn_sw32b(bl + s * 1024, kMsgPlane, 512);
-            mma_tf32(dcol, dal, dbh, idesc, (kb > 0 || s > 0) ? 1u : 0u);
-            mma_tf32(dcol, dah, dbl, idesc, 1u);
-            mma_tf32(dcol, dah, dbh, idesc, 1u);
-          }
-          commit(mbar);
-        }
-        mbar_wait(mbar, parity, ab);
-        parity ^= 1u;
+  if (warp == 8) {
+    // ------------------------------------------------------------------ MMA issuer
+    if (lane == 0) {
+      const uint32_t idesc = idesc_tf32_mn(128, kK);
+      ChunkCursor cc;
+      bool more = cc.first(blockIdx.x, row_ptr, N, gridDim.x);
+      int64_t tile = 0;                                        // tiles issued so far
+      for (int64_t c = 0; more; c++) {
+        const int s = (int)(c & 1);
+        if (!mbar_wait(&full[s], (uint32_t)((c >> 1) & 1), ab)) break;
         fence_after_sync();
+        unsigned char* st = sm + s * kStage;
+        const uint32_t ah = smem_u32(st), al = ah + kVPlane, bh = al + kVPlane, bl = bh + kMsgPlane;
+        const int acc = (int)(tile % kAcc);
+        const uint32_t dcol = tbase + acc * kK;
+        const int nb = min(kEB, cc.deg - cc.kb * kEB);
+        const int nks = (nb + 7) / 8;
+        for (int k = 0; k < nks; k++) {
+          const uint64_t dah = desc_mn_sw32b(ah + k * 1024, kGroup, 512);
+          const uint64_t dal = desc_mn_sw32b(al + k * 1024, kGroup, 512);
+          const uint64_t dbh = desc_mn_sw32b(bh + k * 1024, kMsgPlane, 512);
+          const uint64_t dbl = desc_mn_sw32b(bl + k * 1024, kMsgPlane, 512);
+          mma_tf32(dcol, dal, dbh, idesc, (cc.kb > 0 || k > 0) ? 1u : 0u);
+          mma_tf32(dcol, dah, dbl, idesc, 1u);
+          mma_tf32(dcol, dah, dbh, idesc, 1u);
+        }
+        commit(&empty[s]);
+        if (cc.kb == cc.nkb - 1) {
+          commit(&done[acc]);
+          tile++;
+        }
+        more = cc.next(row_ptr, N, gridDim.x);
       }
-      if (*ab) break;
-      // epilogue of tile T: lane tid = row m = 128 T + tid = x * 16 + b
-      float v[kK];
-      tmem_ld16(tl + T * kK, v);
-      tmem_ld16(tl + T * kK + 16, v + 16);
+    }
+  } else {
+    // ------------------------------------------------------------------ builders (warps 0-7)
+    const int eb = tid & (kEB - 1), quarter = tid >> 6;        // edge row, V group slot of the tile
+    const int ehalf = warp >> 2;                               // epilogue: columns [16 ehalf, +16)
+    const uint32_t tl = tbase + ((uint32_t)((warp & 3) * 32) << 16) + ehalf * 16;
+
+    // store tile t (atom ti, tile index Tt) from accumulator t % kAcc; all 256 builders take part
+    auto store_tile = [&](int64_t t, int64_t ti, int Tt) {
+      const int acc = (int)(t % kAcc);
+      mbar_wait(&done[acc], (uint32_t)((t / kAcc) & 1), ab);
+      fence_after_sync();
+      float v[16];
+      tmem_ld16(tl + acc * kK, v);
       tmem_wait_ld();
       fence_before_sync();
+      // staging: row m (= TMEM lane, 0..127) x 32 k, row stride kStgRow floats, in the 2 x 64 x kStgRow buffer
+      const int m = tid & 127;
+      float* srow = stg + m * kStgRow + ehalf * 16;
 #pragma unroll
-      for (int q = 0; q < kK; q += 4)
-        *reinterpret_cast<float4*>(stg + tid * kStgRow + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
-      __syncthreads();
-      const int nx = T < 2 ? 8 : 4;                     // x planes in this tile
-      for (int q = tid; q < nx * kBK / 4; q += kThreads) {
-        const int xl = q / (kBK / 4), c = q % (kBK / 4); // c: float4 index within the 512-float plane row
-        const int m = xl * 16 + c / 8, kq = (c % 8) * 4;
-        const float4 o = *reinterpret_cast<const float4*>(stg + m * kStgRow + kq);
-        reinterpret_cast<float4*>(D + (8 * T + xl) * plane + i * kBK)[c] = o;
+      for (int q = 0; q < 16; q += 4) *reinterpret_cast<float4*>(srow + q) = make_float4(v[q], v[q + 1], v[q + 2], v[q + 3]);
+      bar_sync(1, 256);
+      const int nx = Tt < 2 ? 8 : 4;
+      for (int q = tid; q < nx * kBK / 4; q += 256) {
+        const int xl = q / (kBK / 4), c = q % (kBK / 4);
+        const int mm = xl * 16 + c / 8, kq = (c % 8) * 4;
+        const float4 o = *reinterpret_cast<const float4*>(stg + mm * kStgRow + kq);
+        reinterpret_cast<float4*>(D + (8 * Tt + xl) * plane + ti * kBK)[c] = o;
+      }
+      bar_sync(1, 256);                                        // staging free again
+    };
+
+    // pending stores: tiles issued but not stored yet (at most kLagT + 1)
+    int64_t pend_atom[kLagT + 1];
+    int pend_T[kLagT + 1];
+    int64_t tiles_built = 0, tiles_stored = 0;
+
+    // operands of one chunk, loaded one chunk ahead (register prefetch) so global latency overlaps the build
+    struct Ops {
+      float p[kB];
+      float y0, y1;
+      float4 mv[2];
+    };
+    auto load_ops = [&](const ChunkCursor& k, Ops& o) {
+      const int nb = min(kEB, k.deg - k.kb * kEB);
+      const int64_t eblk = k.e0 + k.kb * kEB;
+      const bool live = eb < nb;
+      const int64_t e = eblk + eb;
+      const int g = 4 * k.T + quarter;
+#pragma unroll
+      for (int b = 0; b < kB; b += 4) {
+        float4 v = make_float4(0.f, 0.f, 0.f, 0.f);
+        if (live) v = __ldg(reinterpret_cast<const float4*>(phi + e * kB + b));
+        o.p[b] = v.x;
+        o.p[b + 1] = v.y;
+        o.p[b + 2] = v.z;
+        o.p[b + 3] = v.w;
+      }
+      o.y0 = (live && g < 10) ? __ldg(Y + e * kNX + 2 * g) : 0.f;
+      o.y1 = (live && g < 10) ? __ldg(Y + e * kNX + 2 * g + 1) : 0.f;
+#pragma unroll
+      for (int h = 0; h < 2; h++) {                           // msg: 64 rows x 8 quads, 2 per thread
+        const int q = tid + 256 * h, r = q >> 3, cq = q & 7;
+        o.mv[h] = r < nb ? __ldg(reinterpret_cast<const float4*>(msg + (eblk + r) * kK) + cq)
+                         : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+    };
+
+    ChunkCursor cc;
+    bool more = cc.first(blockIdx.x, row_ptr, N, gridDim.x);
+    int64_t last_atom = (int64_t)blockIdx.x - (int64_t)gridDim.x;
+    Ops cur;
+    if (more) load_ops(cc, cur);
+    for (int64_t c = 0; more; c++) {
+      // zero rows for atoms without edges between the previous chunk's atom and this one
+      for (int64_t z = last_atom + gridDim.x; z < cc.i; z += gridDim.x)
+        for (int q = tid; q < kNX * kBK / 4; q += 256) {
+          const int x = q / (kBK / 4), cq = q % (kBK / 4);
+          reinterpret_cast<float4*>(D + x * plane + z * kBK)[cq] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+      last_atom = cc.i;
+      const int s = (int)(c & 1);
+      const int g = 4 * cc.T + quarter;                        // this thread's (x, b) group
+      // MMAs of chunk c-2 done.  No early exit on an abort: the bounded waits then return at once, and every
+      // builder keeps reaching the same named barriers in store_tile
+      if (c >= 2) mbar_wait(&empty[s], (uint32_t)(((c >> 1) - 1) & 1), ab);
+      unsigned char* st = sm + s * kStage;
+      unsigned char* vhi = st;
+      unsigned char* vlo = st + kVPlane;
+      unsigned char* mhi = vlo + kVPlane;
+      unsigned char* mlo = mhi + kMsgPlane;
+      if (g < 10) {
+        unsigned char* gh = vhi + quarter * kGroup;
+        unsigned char* gl = vlo + quarter * kGroup;
+#pragma unroll
+        for (int q = 0; q < 8; q++) {
+          const float y = q < 4 ? cur.y0 : cur.y1;
+          const int b = 4 * (q & 3);
+          const float4 v = make_float4(y * cur.p[b], y * cur.p[b + 1], y * cur.p[b + 2], y * cur.p[b + 3]);
+          *reinterpret_cast<float4*>(gh + sw32b(eb, q)) = split_hi4(v);
+          *reinterpret_cast<float4*>(gl + sw32b(eb, q)) = split_lo4(v);
+        }
+      }
+#pragma unroll
+      for (int h = 0; h < 2; h++) {
+        const int q = tid + 256 * h, r = q >> 3, cq = q & 7;
+        *reinterpret_cast<float4*>(mhi + sw32b(r, cq)) = split_hi4(cur.mv[h]);
+        *reinterpret_cast<float4*>(mlo + sw32b(r, cq)) = split_lo4(cur.mv[h]);
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(&full[s]);
+      const bool tile_end = cc.kb == cc.nkb - 1;
+      const int64_t ci = cc.i;
+      const int cT = cc.T;
+      more = cc.next(row_ptr, N, gridDim.x);
+      if (more) load_ops(cc, cur);                             // next chunk's loads overlap the store below
+      if (tile_end) {                                          // last block of a tile: queue its store
+        pend_atom[tiles_built % (kLagT + 1)] = ci;
+        pend_T[tiles_built % (kLagT + 1)] = cT;
+        tiles_built++;
+        if (tiles_built - tiles_stored > kLagT) {
+          const int pi = (int)(tiles_stored % (kLagT + 1));
+          store_tile(tiles_stored, pend_atom[pi], pend_T[pi]);
+          tiles_stored++;
+        }
       }
     }
-    if (*ab) break;
+    while (tiles_stored < tiles_built) {
+      const int pi = (int)(tiles_stored % (kLagT + 1));
+      store_tile(tiles_stored, pend_atom[pi], pend_T[pi]);
+      tiles_stored++;
+    }
+    // zero rows of trailing atoms without edges
+    for (int64_t z = last_atom + gridDim.x; z < N; z += gridDim.x)
+      for (int q = tid; q < kNX * kBK / 4; q += 256) {
+        const int x = q / (kBK / 4), cq = q % (kBK / 4);
+        reinterpret_cast<float4*>(D + x * plane + z * kBK)[cq] = make_float4(0.f, 0.f, 0.f, 0.f);
+      }
   }
   fence_before_sync();
   __syncthreads();
@@ -214,9 +324,9 @@ __global__ void __launch_bounds__(kThreads, 2)
 int density_tc_xm_fwd(const float* phi, const float* msg, const float* Y, float* D, int64_t N,
                       const int32_t* row_ptr, void* stream) {
   if (N == 0) return FACEK_OK;
-  FACEK_CHECK_ARG((int)kSmem <= max_smem_optin(), "facek_density_tc_xm_fwd: %u B of shared memory needed", kSmem);
-  cudaFuncSetAttribute(dens_fwd_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kSmem);
-  dens_fwd_tc_k<<<grid_for(N, 2), kThreads, kSmem, as_stream(stream)>>>(phi, msg, Y, D, N, 0, row_ptr);
+  FACEK_CHECK_ARG((int)kPSmem <= max_smem_optin(), "facek_density_tc_xm_fwd: %u B of shared memory needed", kPSmem);
+  cudaFuncSetAttribute(dens_fwd_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kPSmem);
+  dens_fwd_tc_k<<<grid_for(N, 1), kPThreads, kPSmem, as_stream(stream)>>>(phi, msg, Y, D, N, 0, row_ptr);
   return launch_status("facek_density_tc_xm_fwd");
 }
 
