@@ -43,6 +43,19 @@ inline int grid_for(int64_t work_blocks, int per_sm) {
   return (int)(g < 1 ? 1 : g);
 }
 
+// d0 += a0 * b0, d1 += a1 * b1 as one paired fp32 FMA (fma.rn.f32x2, sm_100): two round-to-nearest fp32 FMAs,
+// bit-identical to two scalar fmaf calls, in one issue slot
+__device__ __forceinline__ void ffma2(float& d0, float& d1, float a0, float a1, float b0, float b1) {
+  asm("{\n\t.reg .b64 ra, rb, rd;\n\t"
+      "mov.b64 ra, {%2, %3};\n\t"
+      "mov.b64 rb, {%4, %5};\n\t"
+      "mov.b64 rd, {%0, %1};\n\t"
+      "fma.rn.f32x2 rd, ra, rb, rd;\n\t"
+      "mov.b64 {%0, %1}, rd;\n\t}"
+      : "+f"(d0), "+f"(d1)
+      : "f"(a0), "f"(a1), "f"(b0), "f"(b1));
+}
+
 // ---- asynchronous global->shared copies (cp.async, 16-byte chunks; both addresses 16-byte aligned)
 __device__ __forceinline__ void cp_async16(void* smem, const void* gmem) {
   const unsigned s = static_cast<unsigned>(__cvta_generic_to_shared(smem));

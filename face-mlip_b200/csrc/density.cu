@@ -144,8 +144,13 @@ __global__ void __launch_bounds__(256) dens_fwd_k(const T* __restrict__ phi, con
 #pragma unroll
           for (int c = 0; c < TK; c++) {
             const T w = p[a] * m[c];
+            if constexpr (sizeof(T) == 4) {            // paired fp32 FMAs over adjacent components
 #pragma unroll
-            for (int x = 0; x < NX; x++) acc[a][c][x] += w * y[x];
+              for (int x = 0; x < NX; x += 2) ffma2(acc[a][c][x], acc[a][c][x + 1], w, w, y[x], y[x + 1]);
+            } else {
+#pragma unroll
+              for (int x = 0; x < NX; x++) acc[a][c][x] += w * y[x];
+            }
           }
       }
     }
@@ -375,10 +380,7 @@ __global__ void __launch_bounds__(48 * L, L >= 4 ? 4 : 5)
           }
           float t0_ = 0.f, t1 = 0.f;
 #pragma unroll
-          for (int k = 0; k < KH; k += 2) {
-            t0_ += m[k] * g[k];
-            t1 += m[k + 1] * g[k + 1];
-          }
+          for (int k = 0; k < KH; k += 2) ffma2(t0_, t1, m[k], m[k + 1], g[k], g[k + 1]);
           float t = t0_ + t1;
 #pragma unroll
           for (int o = 1; o < L; o <<= 1) t += __shfl_xor_sync(pair_mask, t, o);
@@ -386,7 +388,7 @@ __global__ void __launch_bounds__(48 * L, L >= 4 ? 4 : 5)
           dyx += t * p[b];
           const float w = yx * p[b];
 #pragma unroll
-          for (int k = 0; k < KH; k++) dm[k] += w * g[k];
+          for (int k = 0; k < KH; k += 2) ffma2(dm[k], dm[k + 1], w, w, g[k], g[k + 1]);
         }
         if (half == 0) dY[e * NX + x] = dyx;
       }

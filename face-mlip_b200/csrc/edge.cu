@@ -680,10 +680,8 @@ __global__ void __launch_bounds__(96, 5) transport_bwd_lane_k(const float* __res
           for (int b = 0; b < BB; b++) {
             const float4 d = *reinterpret_cast<const float4*>(rowp + b * Kd);
             dp[b] += (d.x * f[0] + d.y * f[1]) + (d.z * f[2] + d.w * f[3]);
-            P[0] += p[b] * d.x;
-            P[1] += p[b] * d.y;
-            P[2] += p[b] * d.z;
-            P[3] += p[b] * d.w;
+            ffma2(P[0], P[1], p[b], p[b], d.x, d.y);
+            ffma2(P[2], P[3], p[b], p[b], d.z, d.w);
           }
 #pragma unroll
           for (int q = 0; q < 4; q++) {

@@ -198,10 +198,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         const int h = h0 + j;
         float z = pcol[h * np], dz = 0.f;
 #pragma unroll
-        for (int n = 0; n < NB; n++) {
-          z += w1s[h * NB + n] * rb[n];
-          dz += w1s[h * NB + n] * drb[n];
-        }
+        for (int n = 0; n < NB; n++) ffma2(z, dz, w1s[h * NB + n], w1s[h * NB + n], rb[n], drb[n]);
         const float sg = sigmoid(z);
         a[j] = z * sg;
         da1[hh + j] = sg * (1.f + z * (1.f - sg)) * dz;
