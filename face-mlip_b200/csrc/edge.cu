@@ -443,8 +443,13 @@ __global__ void __launch_bounds__(256) transport_fwd_k(const T* __restrict__ phi
 #pragma unroll
           for (int a = 0; a < 4; a++) {
             const T p = sP[t * B + bq * 4 + a];
+            if constexpr (sizeof(T) == 4) {
 #pragma unroll
-            for (int o = 0; o < 18; o++) acc[a][o] += p * f[o];
+              for (int o = 0; o < 18; o += 2) ffma2(acc[a][o], acc[a][o + 1], p, p, f[o], f[o + 1]);
+            } else {
+#pragma unroll
+              for (int o = 0; o < 18; o++) acc[a][o] += p * f[o];
+            }
           }
         }
       }
