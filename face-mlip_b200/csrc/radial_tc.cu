@@ -199,7 +199,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         float z = pcol[h * np], dz = 0.f;
 #pragma unroll
         for (int n = 0; n < NB; n++) ffma2(z, dz, w1s[h * NB + n], w1s[h * NB + n], rb[n], drb[n]);
-        const float sg = sigmoid(z);
+        const float sg = sigmoid_f(z);
         a[j] = z * sg;
         da1[hh + j] = sg * (1.f + z * (1.f - sg)) * dz;
       }
@@ -225,7 +225,7 @@ __global__ void __launch_bounds__(kThreads, 1)
 #pragma unroll
       for (int j = 0; j < 16; j++) {
         const float zz = z[j] + b2s[c0 + j];
-        const float sg = sigmoid(zz);
+        const float sg = sigmoid_f(zz);
         a[j] = zz * sg;
         da2[cc + j] = sg * (1.f + zz * (1.f - sg)) * dz[j];
       }

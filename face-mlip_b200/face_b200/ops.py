@@ -570,7 +570,8 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
         D = DensityMsg.apply(phi, Y, TJ, TI, gr)                                     # 4 x (k_l, N, B*K)
     else:
         D = DensityMsg.apply(phi, Y, msgtab[None], None, gr)
-    s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1)   # (4, N, C)
+    # (4, N, C), contiguous so that A[l] * s[l] (broadcast over the k_l components) runs vectorised
+    s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1).contiguous()
     tpl = {}
     if Gt is not None:
         T1, T2 = Transport.apply(phi, vec, Gt, gr)                                   # (3|6, N, 2*B*Kd)
