@@ -26,10 +26,11 @@ template <typename P>
 struct Planes {
   P base[4];
   int64_t sN, sX;
+  // selects rather than base[rank]: a runtime index into the parameter array would move it to local memory
   __device__ __forceinline__ P at(int64_t i, int x) const {
-    const int r = x < 1 ? 0 : (x < 4 ? 1 : (x < 10 ? 2 : 3));
-    const int o = r == 0 ? 0 : (r == 1 ? 1 : (r == 2 ? 4 : 10));
-    return base[r] + (int64_t)(x - o) * sX + i * sN;
+    const P b = x < 1 ? base[0] : (x < 4 ? base[1] : (x < 10 ? base[2] : base[3]));
+    const int o = x < 1 ? 0 : (x < 4 ? 1 : (x < 10 ? 4 : 10));
+    return b + (int64_t)(x - o) * sX + i * sN;
   }
 };
 
@@ -314,7 +315,9 @@ int launch_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*>
 //   t = sum_k msg[k] g[k] (shuffles join the parts)  ->  dphi[b] += t Y[x],  dY[x] += t phi[b]
 //   dmsg[k] += Y[x] phi[b] g[k]
 // msg and dmsg parts of the edge in registers.  48 edges per round keeps ~90% of the lanes busy at the alloys'
-// ~44 neighbours; five CTAs share an SM, so one CTA's staging overlaps the others' work.
+// ~44 neighbours; five CTAs share an SM, so one CTA's staging overlaps the others' work.  The five G tiles leave
+// the SM's L1 cache only ~28 KB, so per-edge global operands come from L2: each component's Y[e, x] is loaded one
+// iteration ahead, and the message tables of component c + 1 while component c is contracted.
 // With MSG, the lanes also add the message part of dY: msg[e,k] = sum_{c<nc} Y[e,c] (TJ[c,ej,k] + TI[c,ei,k]), so
 // dY[e,c] += sum_k dmsg[e,k] (TJ[c,ej,k] + TI[c,ei,k]) while dmsg is still in registers (TI may be null).
 template <int BB, int KK, int L, bool MSG>
@@ -362,9 +365,12 @@ __global__ void __launch_bounds__(48 * L, L >= 4 ? 4 : 5)
         dp[b] = dp[b + 1] = dp[b + 2] = dp[b + 3] = 0.f;
       }
       const unsigned pair_mask = __activemask();
+      const float* ye = Y + e * NX;
+      float ynext = __ldg(ye);
 #pragma unroll 1
       for (int x = 0; x < NX; x++) {
-        const float yx = __ldg(Y + e * NX + x);
+        const float yx = ynext;
+        if (x + 1 < NX) ynext = __ldg(ye + x + 1);
         const float* gx = sG + x * BK + half * KH;
         float dyx = 0.f;
 #pragma unroll
@@ -404,20 +410,31 @@ __global__ void __launch_bounds__(48 * L, L >= 4 ? 4 : 5)
         const int64_t NKs = N * KK;
         const float* tjb = TJ + (int64_t)ej[e] * KK + half * KH;
         const float* tib = TI ? TI + i * KK + half * KH : nullptr;
+        // tables of component c in (nj, ni), of c + 1 in flight
+        float4 nj[KH / 4], ni[KH / 4];
+#pragma unroll
+        for (int k = 0; k < KH; k += 4) {
+          nj[k / 4] = nc > 0 ? __ldg(reinterpret_cast<const float4*>(tjb + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+          ni[k / 4] = tib && nc > 0 ? __ldg(reinterpret_cast<const float4*>(tib + k)) : make_float4(0.f, 0.f, 0.f, 0.f);
+        }
 #pragma unroll 1
         for (int c = 0; c < nc; c++) {
+          float4 a[KH / 4];
+#pragma unroll
+          for (int q = 0; q < KH / 4; q++)
+            a[q] = make_float4(nj[q].x + ni[q].x, nj[q].y + ni[q].y, nj[q].z + ni[q].z, nj[q].w + ni[q].w);
+          if (c + 1 < nc) {
+#pragma unroll
+            for (int k = 0; k < KH; k += 4) {
+              nj[k / 4] = __ldg(reinterpret_cast<const float4*>(tjb + (c + 1) * NKs + k));
+              if (tib) ni[k / 4] = __ldg(reinterpret_cast<const float4*>(tib + (c + 1) * NKs + k));
+            }
+          }
           float sc = 0.f;
 #pragma unroll
           for (int k = 0; k < KH; k += 4) {
-            float4 a = __ldg(reinterpret_cast<const float4*>(tjb + c * NKs + k));
-            if (tib) {
-              const float4 t = __ldg(reinterpret_cast<const float4*>(tib + c * NKs + k));
-              a.x += t.x;
-              a.y += t.y;
-              a.z += t.z;
-              a.w += t.w;
-            }
-            sc += (dm[k] * a.x + dm[k + 1] * a.y) + (dm[k + 2] * a.z + dm[k + 3] * a.w);
+            const float4 v = a[k / 4];
+            sc += (dm[k] * v.x + dm[k + 1] * v.y) + (dm[k + 2] * v.z + dm[k + 3] * v.w);
           }
 #pragma unroll
           for (int o = 1; o < L; o <<= 1) sc += __shfl_xor_sync(pair_mask, sc, o);
