@@ -7,16 +7,20 @@
 // packed once (facek_gemm_pack) into an "image": for every N tile (Nt columns) and every 32-wide K chunk, a tf32
 // hi plane and a lo plane in the K-major no-swizzle operand layout.
 //
-// Warp roles (352 threads; each single-thread role has a warp of its own so that no role's waits stall another):
+// Warp roles (384 threads; each single-thread role has a warp of its own so that no role's waits stall another):
 //   warp 8, lane 0     A producer: per K chunk one TMA 2D load of the 128 x 32 fp32 A tile into a 128-byte-
 //                      swizzled K-major stage of a deep ring (the hi operand as the tensor core reads raw fp32);
 //   warp 9, lane 0     W producer: one bulk copy of the chunk's W image into a shallow ring (L2-resident data);
 //                      stages complete on "full" mbarriers and are reused after the MMAs that read them commit
 //                      to their "empty" mbarriers, so the HBM stream runs SA - 1 chunks ahead of the MMAs.
-//   warp 10, lane 0    MMA issuer: once all 256 compute threads have arrived on the chunk's "split" mbarrier and
-//                      its W chunk has landed, 4 K-steps x 3 split terms of M=128 x N=Nt x K=8 MMAs into one of
-//                      four TMEM partials, then commits to the partial's, the A stage's and the W stage's
-//                      mbarriers.
+//   warps 10, 11,      MMA issuers, even and odd chunks: once all 256 compute threads have arrived on the chunk's
+//   lane 0             "split" mbarrier and its A and W chunks have landed, 4 K-steps x 3 split terms of M=128 x
+//                      N=Nt x K=8 MMAs into one of four TMEM partials, then commits to the partial's, the A
+//                      stage's and the W stage's mbarriers.  The MMA queue holds only a few instructions and each
+//                      issuer's three barrier checks take several hundred cycles, so with one issuer the tensor
+//                      pipe idled while it checked; with two, one issuer's checks overlap the other's MMAs.  Each
+//                      chunk owns its partial, lo plane and ring stages, and a commit tracks only the issuing
+//                      thread's MMAs, so the two need no ordering between them.
 //   warps 0-7          split: lo = tf32(x - trunc(x)) into one of four lo planes (same swizzle), arrive; the
 //                      partial of the chunk three behind is loaded from TMEM while the split runs and folded into
 //                      fp32 registers; a finished tile leaves through padded shared memory as coalesced
@@ -40,7 +44,7 @@ using namespace tc;
 constexpr int kM = 128;                       // rows per tile (MMA M)
 constexpr int kKc = 32;                       // K chunk (fp32 elements) = one 128-byte swizzle row
 constexpr int kCompute = 256;                 // warps 0-7
-constexpr int kThr = kCompute + 96;           // + A producer, W producer and MMA issuer warps
+constexpr int kThr = kCompute + 128;          // + A producer, W producer and two MMA issuer warps
 constexpr uint32_t kPlane = kM * kKc * 4;     // one 128 x 32 fp32 operand plane (16 KB)
 
 struct GemmArgs {
@@ -198,10 +202,10 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUt
                   &fullW[s]);
         pc.next(g.k_chunks, g.n_tiles, gridDim.x);
       }
-    } else if (warp == 10 && lane == 0) {
-      // ---------------------------------------------------------------- MMA issuer
+    } else if (warp >= 10 && lane == 0) {
+      // ---------------------------------------------------------------- MMA issuers (warp 10 even, 11 odd chunks)
       const uint32_t idesc = idesc_tf32(kM, Nt);
-      for (int64_t j = 0; j < total; j++) {
+      for (int64_t j = warp - 10; j < total; j += 2) {
         const int sa = (int)(j % SA), sw = (int)(j % SW), b = (int)(j % kNB);
         if (!mbar_wait(&fullA[sa], (uint32_t)((j / SA) & 1), ab)) break;       // A tile landed (TMA)
         if (!mbar_wait(&split_bar[b], (uint32_t)((j / kNB) & 1), ab)) break;   // lo plane written
