@@ -30,6 +30,9 @@ ROOT = os.path.dirname(os.path.abspath(__file__))
 for p in (ROOT, os.path.join(ROOT, "face-mlip_b200")):
     if p not in sys.path:
         sys.path.insert(0, p)
+# the full-size step peaks at ~150 GiB of the GPU's 178 in buffers of up to tens of GiB; growable segments keep
+# the caching allocator from failing on fragmentation (set before torch initialises CUDA)
+os.environ.setdefault("PYTORCH_CUDA_ALLOC_CONF", "expandable_segments:True")
 
 import torch  # noqa: E402
 

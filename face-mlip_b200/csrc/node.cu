@@ -599,6 +599,108 @@ int eng_bwd(const void* y1, const void* y2, const void* y3, const void* a, const
 
 using namespace facek;
 
+// ---- per-atom broadcast scaling x[j, n, c] * s[n, c] over the J components of a Cartesian rank
+// (face-mlip face/model.py:183-186 and :200-201 moment scaling by the element scale / <neighbours>,
+// :277-295 the gates of the equivariant products).  s may be a column slice of a wider row (row stride lds).
+// Forward out = x * s; adjoint dx = g * s and, when wanted, ds[n, c] = sum_j g[j, n, c] x[j, n, c].
+namespace facek {
+namespace {
+template <typename T>
+__global__ void bcast_mul_k(const T* __restrict__ x, const T* __restrict__ s, T* __restrict__ out, int J, int64_t N,
+                            int C, int64_t lds) {
+  const int64_t NC = N * C;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < NC; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = q / C;
+    const T sv = s[n * lds + (q - n * C)];
+    for (int j = 0; j < J; j++) out[j * NC + q] = x[j * NC + q] * sv;
+  }
+}
+// fp32, C % 4 == 0 and 16-byte aligned rows: four channels per thread
+__global__ void bcast_mul4_k(const float4* __restrict__ x, const float* __restrict__ s, float4* __restrict__ out,
+                             int J, int64_t N, int C4, int64_t lds) {
+  const int64_t NC4 = N * C4;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < NC4; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = q / C4;
+    const float4 sv = *reinterpret_cast<const float4*>(s + n * lds + 4 * (q - n * C4));
+#pragma unroll 2
+    for (int j = 0; j < J; j++) {
+      const float4 v = x[j * NC4 + q];
+      out[j * NC4 + q] = make_float4(v.x * sv.x, v.y * sv.y, v.z * sv.z, v.w * sv.w);
+    }
+  }
+}
+template <typename T>
+__global__ void bcast_mul_bwd_k(const T* __restrict__ g, const T* __restrict__ x, const T* __restrict__ s,
+                                T* __restrict__ dx, T* __restrict__ ds, int J, int64_t N, int C, int64_t lds) {
+  const int64_t NC = N * C;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < NC; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = q / C;
+    const T sv = s[n * lds + (q - n * C)];
+    T acc = 0;
+    for (int j = 0; j < J; j++) {
+      const T gv = g[j * NC + q];
+      dx[j * NC + q] = gv * sv;
+      if (ds) acc += gv * x[j * NC + q];
+    }
+    if (ds) ds[q] = acc;
+  }
+}
+__global__ void bcast_mul_bwd4_k(const float4* __restrict__ g, const float4* __restrict__ x,
+                                 const float* __restrict__ s, float4* __restrict__ dx, float4* __restrict__ ds, int J,
+                                 int64_t N, int C4, int64_t lds) {
+  const int64_t NC4 = N * C4;
+  for (int64_t q = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; q < NC4; q += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t n = q / C4;
+    const float4 sv = *reinterpret_cast<const float4*>(s + n * lds + 4 * (q - n * C4));
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+    for (int j = 0; j < J; j++) {
+      const float4 gv = g[j * NC4 + q];
+      dx[j * NC4 + q] = make_float4(gv.x * sv.x, gv.y * sv.y, gv.z * sv.z, gv.w * sv.w);
+      if (ds) {
+        const float4 xv = x[j * NC4 + q];
+        acc.x += gv.x * xv.x;
+        acc.y += gv.y * xv.y;
+        acc.z += gv.z * xv.z;
+        acc.w += gv.w * xv.w;
+      }
+    }
+    if (ds) ds[q] = acc;
+  }
+}
+bool vec4_ok(const void* a, const void* b, const void* c, const void* d, int C, int64_t lds) {
+  const uintptr_t m = reinterpret_cast<uintptr_t>(a) | reinterpret_cast<uintptr_t>(b) |
+                      reinterpret_cast<uintptr_t>(c) | reinterpret_cast<uintptr_t>(d);
+  return (m & 15) == 0 && C % 4 == 0 && lds % 4 == 0;
+}
+template <typename T>
+int bcast_fwd(const void* x, const void* s, void* out, int J, int64_t N, int C, int64_t lds, void* stream) {
+  if (std::is_same<T, float>::value && vec4_ok(x, s, out, nullptr, C, lds)) {
+    const int64_t n4 = N * (C / 4);
+    bcast_mul4_k<<<grid_for(ceil_div<int64_t>(n4, 256), 8), 256, 0, as_stream(stream)>>>(
+        (const float4*)x, (const float*)s, (float4*)out, J, N, C / 4, lds);
+  } else {
+    bcast_mul_k<T><<<grid_for(ceil_div<int64_t>(N * C, 256), 8), 256, 0, as_stream(stream)>>>(
+        (const T*)x, (const T*)s, (T*)out, J, N, C, lds);
+  }
+  return launch_status("facek_bcast_mul_fwd");
+}
+template <typename T>
+int bcast_bwd(const void* g, const void* x, const void* s, void* dx, void* ds, int J, int64_t N, int C, int64_t lds,
+              void* stream) {
+  if (std::is_same<T, float>::value && vec4_ok(g, s, dx, ds ? x : nullptr, C, lds) &&
+      (reinterpret_cast<uintptr_t>(ds) & 15) == 0) {
+    const int64_t n4 = N * (C / 4);
+    bcast_mul_bwd4_k<<<grid_for(ceil_div<int64_t>(n4, 256), 8), 256, 0, as_stream(stream)>>>(
+        (const float4*)g, (const float4*)x, (const float*)s, (float4*)dx, (float4*)ds, J, N, C / 4, lds);
+  } else {
+    bcast_mul_bwd_k<T><<<grid_for(ceil_div<int64_t>(N * C, 256), 8), 256, 0, as_stream(stream)>>>(
+        (const T*)g, (const T*)x, (const T*)s, (T*)dx, (T*)ds, J, N, C, lds);
+  }
+  return launch_status("facek_bcast_mul_bwd");
+}
+}  // namespace
+}  // namespace facek
+
 extern "C" int facek_node_fwd(int dtype, const void* P1, const void* Q1, const void* S1, const void* P2, const void* Q2,
                               const void* S2, const void* P3, const void* Q3, const void* a, const void* b, void* inv,
                               void* V, void* Mf, int64_t N, int32_t C, int32_t eq, void* stream) {
@@ -640,4 +742,24 @@ extern "C" int facek_node_engine_bwd(int dtype, const void* y0, const void* y1, 
   FACEK_CHECK_ARG(!eq || (a && b && gV && gMs), "facek_node_engine_bwd: eq=1 needs a, b, gV, gMs");
   return FACEK_DISPATCH(dtype, eng_bwd, y1, y2, y3, a, b, g_inv9, gV, gMs, dy0, dy1, dy2, dy3, N, C, eq, max_body,
                         stream);
+}
+
+extern "C" int facek_bcast_mul_fwd(int dtype, const void* x, const void* s, void* out, int32_t J, int64_t N, int32_t C,
+                                   int64_t lds, void* stream) {
+  FACEK_CHECK_ARG(J >= 0 && N >= 0 && C > 0 && lds >= C, "facek_bcast_mul_fwd: bad sizes J=%d N=%lld C=%d lds=%lld", J,
+                  (long long)N, C, (long long)lds);
+  if (J == 0 || N == 0) return FACEK_OK;
+  FACEK_CHECK_ARG(x && s && out, "facek_bcast_mul_fwd: null tensor");
+  return FACEK_DISPATCH(dtype, bcast_fwd, x, s, out, J, N, C, lds, stream);
+}
+
+extern "C" int facek_bcast_mul_bwd(int dtype, const void* g, const void* x, const void* s, void* dx, void* ds,
+                                   int32_t J, int64_t N, int32_t C, int64_t lds, void* stream) {
+  FACEK_CHECK_ARG(J >= 0 && N >= 0 && C > 0 && lds >= C, "facek_bcast_mul_bwd: bad sizes J=%d N=%lld C=%d lds=%lld", J,
+                  (long long)N, C, (long long)lds);
+  if (N == 0) return FACEK_OK;
+  // J == 0: no components (empty g, x, dx may be null); ds, when wanted, is zeroed
+  FACEK_CHECK_ARG(s && ((g && dx) || J == 0), "facek_bcast_mul_bwd: null tensor");
+  FACEK_CHECK_ARG(!ds || x || J == 0, "facek_bcast_mul_bwd: ds needs x");
+  return FACEK_DISPATCH(dtype, bcast_bwd, g, x, s, dx, ds, J, N, C, lds, stream);
 }

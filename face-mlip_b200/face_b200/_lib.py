@@ -29,6 +29,8 @@ SIGNATURES = {
     "facek_node_bwd": [I32] + [P] * 23 + [I64, I32, I32, P],
     "facek_node_engine_fwd": [I32] + [P] * 9 + [I64, I32, I32, I32, P],
     "facek_node_engine_bwd": [I32] + [P] * 13 + [I64, I32, I32, I32, P],
+    "facek_bcast_mul_fwd": [I32, P, P, P, I32, I64, I32, I64, P],
+    "facek_bcast_mul_bwd": [I32, P, P, P, P, P, I32, I64, I32, I64, P],
     "facek_nlist_cell_workspace": [I64, PD, D, PI64],
     "facek_nlist_cell_count": [P, I64, PD, D, P, P, P],
     "facek_nlist_cell_fill": [I32, P, I64, PD, D, P, P, P, P, P, P, P],

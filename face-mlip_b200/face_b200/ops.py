@@ -251,6 +251,33 @@ class Transport(torch.autograd.Function):
         return dphi, dvec, dGt, None
 
 
+class BcastMul(torch.autograd.Function):
+    """x (J, N, C) * s (N, C) broadcast over the J components (face/model.py:183-186 moment scaling, :277-295 gates);
+    s may be a column slice of a wider (N, lds) row."""
+
+    @staticmethod
+    def forward(ctx, x, s):
+        J, N, C = x.shape
+        x = x.contiguous()
+        if s.stride(1) != 1 or s.stride(0) < C:
+            s = s.contiguous()
+        out = torch.empty_like(x)
+        _lib.call("facek_bcast_mul_fwd", _tag(x), _p(x), _p(s), _p(out), J, N, C, s.stride(0), _lib.stream())
+        ctx.save_for_backward(x if ctx.needs_input_grad[1] else None, s)
+        return out
+
+    @staticmethod
+    def backward(ctx, g):
+        x, s = ctx.saved_tensors
+        J, N, C = g.shape
+        g = g.contiguous()
+        dx = torch.empty_like(g)
+        ds = torch.empty(N, C, dtype=g.dtype, device=g.device) if x is not None else None
+        _lib.call("facek_bcast_mul_bwd", _tag(g), _p(g), _p(x) if x is not None else None, _p(s), _p(dx),
+                  _p(ds) if ds is not None else None, J, N, C, s.stride(0), _lib.stream())
+        return dx, ds
+
+
 class NodeAlgebraEngine(torch.autograd.Function):
     """Invariant families + gated products from the (N, k_l, 3C) projections."""
 
@@ -503,6 +530,8 @@ def prepare(model, dtype, dev):
             q["pvtT"] = _lin(model, blk.pvt, dtype, dev)[0].t().contiguous()                # (cprev, nt*Kd)
             q["pmtT"] = _lin(model, blk.pmt, dtype, dev)[0].t().contiguous()
             q["y2w"] = torch.tensor(Y2W, dtype=dtype, device=dev)[:, None, None]
+            # the y2 weights folded into per-component maps: (Md @ w) * y2w == Md @ (w * y2w), one batched matmul
+            q["dir_y2"] = [q["y2w"] * q["dir"][i] for i in (1, 3)]                            # each (6, Kd, K)
         if blk.transport:
             for name in ("tmix1", "tmix2"):
                 w = _lin(model, getattr(blk, name), dtype, dev)[0]                           # (C, B*2*Kd) cols (b,t,kd)
@@ -563,21 +592,21 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
         Mb = src2 @ q["pmtT"]                                                        # (6, N, nt*Kd)
         Vd, Md = Vb[..., :Kd], Mb[..., :Kd]
         w1, w2, w3, w4 = q["dir"]
-        TJ = torch.cat([(msgtab + q["dir_b"])[None], Vd @ w1, (Md @ w2) * q["y2w"]], 0)        # (10, N, K)
-        TI = torch.cat([torch.zeros_like(msgtab)[None], Vd @ w3, (Md @ w4) * q["y2w"]], 0)
+        w2y, w4y = q["dir_y2"]
+        TJ = torch.cat([(msgtab + q["dir_b"])[None], Vd @ w1, Md @ w2y], 0)                  # (10, N, K)
+        TI = torch.cat([torch.zeros_like(msgtab)[None], Vd @ w3, Md @ w4y], 0)
         if q["transport"]:
             Gt = torch.cat([Vb[..., Kd:], Mb[..., Kd:]], 0)                           # (9, N, Kd)
         D = DensityMsg.apply(phi, Y, TJ, TI, gr)                                     # 4 x (k_l, N, B*K)
     else:
         D = DensityMsg.apply(phi, Y, msgtab[None], None, gr)
-    # (4, N, C), contiguous so that A[l] * s[l] (broadcast over the k_l components) runs vectorised
-    s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1).contiguous()
+    s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1).contiguous()   # (4, N, C)
     tpl = {}
     if Gt is not None:
         T1, T2 = Transport.apply(phi, vec, Gt, gr)                                   # (3|6, N, 2*B*Kd)
         tpl = {1: (T1, q["tmix1T"], q["tmix1D"]), 2: (T2, q["tmix2T"], q["tmix2D"])}
     A = [mm(D[l], q["mixT"][l], q["mixD"][l], *tpl.get(l, (None, None, None))) for l in range(4)]   # (k_l, N, C)
-    A = [A[l] * s[l] for l in range(4)]
+    A = [BcastMul.apply(A[l], s[l]) for l in range(4)]
     # invariants (face/model.py:204-270): projections straight into the node kernel's layout
     sets = A_sets + [A]
     ys = [mm(torch.cat([a[l] for a in sets], 2), q["projT"][l], q["projD"][l]) for l in range(4)]   # (k_l, N, 3C)
@@ -594,7 +623,7 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
     eq_new = None
     if q["eq_out"]:
         gv, gm = linear(inv, q["gate"], q["gateD"]).chunk(2, dim=-1)
-        eq_new = (V * gv[None], Ms * gm[None])
+        eq_new = (BcastMul.apply(V, gv), BcastMul.apply(Ms, gm))
     return o[:, 0], h + o[:, 1:], A, eq_new
 
 

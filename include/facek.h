@@ -90,6 +90,15 @@ int facek_node_engine_bwd(int dtype, const void* y0, const void* y1, const void*
                           const void* b, const void* g_inv9, const void* gV, const void* gMs, void* dy0, void* dy1,
                           void* dy2, void* dy3, int64_t N, int32_t C, int32_t eq, int32_t max_body, void* stream);
 
+/* Per-atom broadcast scaling over the J components of one Cartesian rank, engine layout (J, N, C):
+ * out[j,n,c] = x[j,n,c] * s[n*lds + c] -- the moment scaling by elem_scale / <neighbours> (face/model.py:183-186,
+ * :200-201) and the gates of the equivariant products (face/model.py:277-295); s may be a column slice (lds >= C).
+ * Backward: dx = g * s and, when ds is non-null, ds[n,c] = sum_j g[j,n,c] x[j,n,c] (dense (N, C)). */
+int facek_bcast_mul_fwd(int dtype, const void* x, const void* s, void* out, int32_t J, int64_t N, int32_t C,
+                        int64_t lds, void* stream);
+int facek_bcast_mul_bwd(int dtype, const void* g, const void* x, const void* s, void* dx, void* ds, int32_t J,
+                        int64_t N, int32_t C, int64_t lds, void* stream);
+
 /* ---------------------------------------------------------------------------------------------------
  * Neighbour list (cell list, fp64 distance test), replacing ase.neighborlist.neighbor_list("ijS") as called at
  * face-mlip face/neighbors.py:12 and face/datasets.py:51 (+ the stable argsort and slot fill :14, :74-79).

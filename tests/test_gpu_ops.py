@@ -425,3 +425,34 @@ def test_density_xm_bwd_fp32_ragged_rows():
     for u, v in zip(out[torch.float32], out[torch.float64]):
         assert torch.isfinite(u).all()
         assert rel(u.double(), v) < 1e-5
+
+
+@pytest.mark.parametrize("dtype", [torch.float32, torch.float64])
+@pytest.mark.parametrize("J,N,C,lds", [(1, 1000, 64, 64), (10, 3001, 64, 128), (6, 257, 6, 6), (3, 50, 8, 11), (0, 5, 4, 4)])
+def test_bcast_mul_matches_torch(dtype, J, N, C, lds):
+    """facek_bcast_mul_fwd/bwd (moment scaling and gates, face/model.py:183-186, :277-295) against torch: exact in
+    the forward and dx (one product each), ds within rounding of a J-term sum; s as a column slice of wider rows."""
+    from face_b200 import _lib
+    from face_b200.ops import BcastMul
+    g = torch.Generator(device="cuda").manual_seed(J * 7 + C)
+    x = torch.randn(J, N, C, dtype=dtype, device="cuda", generator=g, requires_grad=True)
+    wide = torch.randn(N, lds, dtype=dtype, device="cuda", generator=g)
+    s = wide[:, :C].requires_grad_(False)
+    s_req = s.clone().requires_grad_(True)
+    y = BcastMul.apply(x, s_req)
+    assert torch.equal(y, x * s_req[None])
+    G = torch.randn_like(y)
+    dx, ds = torch.autograd.grad((y * G).sum(), (x, s_req))
+    assert torch.equal(dx, G * s_req[None])
+    tol = 1e-5 if dtype == torch.float32 else 1e-13
+    ref = (G * x).sum(0)
+    assert (ds - ref).abs().max() <= tol * max(1.0, float(ref.abs().max()))
+    # column slice without a copy (lds > C) and without ds
+    out = torch.empty(J, N, C, dtype=dtype, device="cuda")
+    _lib.call("facek_bcast_mul_fwd", _lib.dtype_tag(x), _lib.ptr(x.detach()), _lib.ptr(s), _lib.ptr(out), J, N, C,
+              lds, _lib.stream())
+    assert torch.equal(out, x.detach() * s[None])
+    dx2 = torch.empty_like(out)
+    _lib.call("facek_bcast_mul_bwd", _lib.dtype_tag(x), _lib.ptr(G), None, _lib.ptr(s), _lib.ptr(dx2), None, J, N, C,
+              lds, _lib.stream())
+    assert torch.equal(dx2, G * s[None])
