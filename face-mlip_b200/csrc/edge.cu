@@ -601,8 +601,10 @@ __global__ void __launch_bounds__(256) transport_bwd_k(const T* __restrict__ phi
 
 // Transport backward, two lanes per edge (fp32, B = BB, Kd a multiple of 8).  A 96-thread CTA takes one row (atom)
 // at a time and stages its 18 gradient rows dT[o, i] (BB x Kd each) in shared memory.  Each lane of an edge's pair
-// takes half of the kd channels; for each group of 4 it keeps g = Gt[:, j, kd..kd+3] (9 x 4), walks the 18
-// outputs o and for each the BB rows dT[o, i, b, kd..kd+3] (16-byte broadcast reads):
+// takes half of the kd channels; for each group of KQ = 2 it keeps g = Gt[:, j, kd..kd+1] (9 x 2), walks the 18
+// outputs o and for each the BB rows dT[o, i, b, kd..kd+1] (8-byte broadcast reads; groups of 2 rather than 4 keep
+// the live set under the 128-register cap of five CTAs per SM and the unrolled walk small enough for the
+// instruction cache):
 //   dphi[b] += dT . f_o,   P_o = sum_b phi[b] dT   ->   folded at once into dV, dM (per kd) and du
 // and the pair adds its dphi and du halves with shuffles.  Same outputs as transport_bwd_k.  96 lanes = 48 edges
 // per round (rows with more edges loop).
@@ -618,6 +620,7 @@ __global__ void __launch_bounds__(96, 5) transport_bwd_lane_k(const float* __res
                                                               int acc, float* __restrict__ dGe, int64_t N, int Kd) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   float* sD = reinterpret_cast<float*>(smem_raw);              // [o][b][kd], o in output order
+  constexpr int KQ = 2;                                         // kd channels per group
   const int tid = threadIdx.x, half = tid & 1, slot = tid >> 1;
   const int BKd = BB * Kd;
   for (int64_t i = blockIdx.x; i < N; i += gridDim.x) {
@@ -639,7 +642,7 @@ __global__ void __launch_bounds__(96, 5) transport_bwd_lane_k(const float* __res
       const float vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
       const float r = sqrtf(vx * vx + vy * vy + vz * vz);
       const float u[3] = {vx / r, vy / r, vz / r};
-      float p[BB], dp[BB];
+      float p[BB], dp[BB][2];                                   // dp[b] as two partial sums (paired FMAs)
 #pragma unroll
       for (int b = 0; b < BB; b += 4) {
         const float4 v = __ldg(reinterpret_cast<const float4*>(phi + e * BB + b));
@@ -647,28 +650,26 @@ __global__ void __launch_bounds__(96, 5) transport_bwd_lane_k(const float* __res
         p[b + 1] = v.y;
         p[b + 2] = v.z;
         p[b + 3] = v.w;
-        dp[b] = dp[b + 1] = dp[b + 2] = dp[b + 3] = 0.f;
+#pragma unroll
+        for (int q = 0; q < 4; q++) dp[b + q][0] = dp[b + q][1] = 0.f;
       }
       float du[3] = {0.f, 0.f, 0.f};
       const int kh = Kd / 2;
 #pragma unroll 1
-      for (int k0 = half * kh; k0 < half * kh + kh; k0 += 4) {
-        float g[9][4], dG[9][4];
+      for (int k0 = half * kh; k0 < half * kh + kh; k0 += KQ) {
+        float g[9][KQ], dG[9][KQ];
 #pragma unroll
         for (int c = 0; c < 9; c++) {
-          const float4 v = __ldg(reinterpret_cast<const float4*>(Gt + ((int64_t)c * N + j) * Kd + k0));
+          const float2 v = __ldg(reinterpret_cast<const float2*>(Gt + ((int64_t)c * N + j) * Kd + k0));
           g[c][0] = v.x;
           g[c][1] = v.y;
-          g[c][2] = v.z;
-          g[c][3] = v.w;
-#pragma unroll
-          for (int q = 0; q < 4; q++) dG[c][q] = 0.f;
+          dG[c][0] = dG[c][1] = 0.f;
         }
 #pragma unroll
         for (int o = 0; o < 18; o++) {
-          float f[4];
+          float f[KQ];
 #pragma unroll
-          for (int q = 0; q < 4; q++) {
+          for (int q = 0; q < KQ; q++) {
             if (o < 3) f[q] = g[o][q];
             else if (o < 6) {
               const int a = o - 3;
@@ -680,16 +681,15 @@ __global__ void __launch_bounds__(96, 5) transport_bwd_lane_k(const float* __res
             }
           }
           const float* rowp = sD + o * BKd + k0;
-          float P[4] = {0.f, 0.f, 0.f, 0.f};
+          float P[KQ] = {0.f, 0.f};
 #pragma unroll
           for (int b = 0; b < BB; b++) {
-            const float4 d = *reinterpret_cast<const float4*>(rowp + b * Kd);
-            dp[b] += (d.x * f[0] + d.y * f[1]) + (d.z * f[2] + d.w * f[3]);
+            const float2 d = *reinterpret_cast<const float2*>(rowp + b * Kd);
+            ffma2(dp[b][0], dp[b][1], d.x, d.y, f[0], f[1]);
             ffma2(P[0], P[1], p[b], p[b], d.x, d.y);
-            ffma2(P[2], P[3], p[b], p[b], d.z, d.w);
           }
 #pragma unroll
-          for (int q = 0; q < 4; q++) {
+          for (int q = 0; q < KQ; q++) {
             const float w = P[q];
             if (o < 3) dG[o][q] += w;
             else if (o < 6) {
@@ -716,18 +716,21 @@ __global__ void __launch_bounds__(96, 5) transport_bwd_lane_k(const float* __res
         }
         float* dg = dGe + e * 9 * (int64_t)Kd + k0;
 #pragma unroll
-        for (int c = 0; c < 9; c++)
-          *reinterpret_cast<float4*>(dg + c * Kd) = make_float4(dG[c][0], dG[c][1], dG[c][2], dG[c][3]);
+        for (int c = 0; c < 9; c++) *reinterpret_cast<float2*>(dg + c * Kd) = make_float2(dG[c][0], dG[c][1]);
       }
       const unsigned pm = __activemask();
+      float dps[BB];
 #pragma unroll
-      for (int b = 0; b < BB; b++) dp[b] += __shfl_xor_sync(pm, dp[b], 1);
+      for (int b = 0; b < BB; b++) {
+        dps[b] = dp[b][0] + dp[b][1];
+        dps[b] += __shfl_xor_sync(pm, dps[b], 1);
+      }
 #pragma unroll
       for (int d = 0; d < 3; d++) du[d] += __shfl_xor_sync(pm, du[d], 1);
       if (half) continue;
 #pragma unroll
       for (int b = 0; b < BB; b += 4)
-        *reinterpret_cast<float4*>(dphi + e * BB + b) = make_float4(dp[b], dp[b + 1], dp[b + 2], dp[b + 3]);
+        *reinterpret_cast<float4*>(dphi + e * BB + b) = make_float4(dps[b], dps[b + 1], dps[b + 2], dps[b + 3]);
       float dx, dy, dz;
       unit_bwd(u[0], u[1], u[2], r, du[0], du[1], du[2], dx, dy, dz);
       if (acc) {
