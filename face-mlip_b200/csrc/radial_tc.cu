@@ -13,9 +13,12 @@
 // so one group's CUDA-core work overlaps the other's MMAs (16 warps per SM hide the CUDA-core latencies).  The
 // pair embedding is kept transposed, [hidden][pair] with b1 folded in, so lanes with different element pairs read
 // different banks.  The MMAs run kind::tf32 with the 3-term split,
-// which keeps fp32 accuracy (tc.cuh). Weights are split once per CTA into shared memory; the CTA is persistent
-// over tiles. Tensor memory: 128 fp32 columns per group (value and tangent accumulators of W2, later reused
-// for W3).
+// which keeps fp32 accuracy (tc.cuh). Weights are split once per CTA into shared memory, as one operand of 2R rows
+// per layer (lo parts in rows 0 .. R-1, hi parts in rows R .. 2R-1); an MMA costs about the same for any N up to
+// 128, so each K step issues two instead of three:
+//   [D_s | D_b] (=|+)= A_hi . [W_lo | W_hi]  (N = 2R),   D_s += A_lo . W_hi  (N = R),   result D_s + D_b.
+// The CTA is persistent over tiles. Tensor memory: 256 fp32 columns per group (value and tangent accumulators
+// of W2, 2 x 64 each; later reused for W3).
 #include "common.cuh"
 #include "radial.cuh"
 #include "tc.cuh"
@@ -29,7 +32,7 @@ constexpr int kH = 64;                               // hidden width
 constexpr int kRows = 128;                           // edges per warpgroup tile = MMA M
 constexpr int kThreads = 512;                        // two groups of 8 warps (2 threads per edge row)
 constexpr uint32_t kPlane = kRows * kH * 4;          // one fp32 operand plane (32 KB)
-constexpr uint32_t kTmemCols = 256;
+constexpr uint32_t kTmemCols = 512;
 
 struct Layout {
   uint32_t a, w2, w3, w1, b1, b2, b3, pair, mbar, slot, abort_, total;
@@ -38,8 +41,8 @@ struct Layout {
 __host__ __device__ inline Layout layout_for(int NB, int BO, int n_el) {
   Layout L;
   L.a = 0;                                            // [wg][hi|lo] operand planes
-  L.w2 = L.a + 4 * kPlane;                            // W2 hi, lo (64 x 64)
-  L.w3 = L.w2 + 2 * kH * kH * 4;                      // W3 hi, lo (BO x 64)
+  L.w2 = L.a + 4 * kPlane;                            // W2 [lo | hi] (2 x 64 rows x 64)
+  L.w3 = L.w2 + 2 * kH * kH * 4;                      // W3 [lo | hi] (2 x BO rows x 64)
   L.w1 = L.w3 + 2 * BO * kH * 4;                      // W1 (64 x NB), zero-padded basis
   L.b1 = L.w1 + kH * NB * 4;
   L.b2 = L.b1 + kH * 4;
@@ -76,18 +79,16 @@ __global__ void __launch_bounds__(kThreads, 1)
   const int half = wt >> 7;                          // hidden units [32 half, 32 half + 32) of this thread's row
   const int np = n_el * n_el;
 
-  // ---- weights -> shared memory (W2, W3 as tf32 hi/lo planes in the K-major operand layout)
+  // ---- weights -> shared memory (W2, W3 as [lo | hi] tf32 rows in the K-major operand layout)
   for (int q = tid; q < kH * kH; q += kThreads) {
     const float w = w2[q], hi = to_tf32(w);
-    const uint32_t off = kmajor_off(q / kH, q % kH, kH);
-    *reinterpret_cast<float*>(w2s + off) = hi;
-    *reinterpret_cast<float*>(w2s + kH * kH * 4 + off) = to_tf32(w - hi);
+    *reinterpret_cast<float*>(w2s + kmajor_off(q / kH, q % kH, 2 * kH)) = to_tf32(w - hi);
+    *reinterpret_cast<float*>(w2s + kmajor_off(kH + q / kH, q % kH, 2 * kH)) = hi;
   }
   for (int q = tid; q < BO * kH; q += kThreads) {
     const float w = w3[q], hi = to_tf32(w);
-    const uint32_t off = kmajor_off(q / kH, q % kH, BO);
-    *reinterpret_cast<float*>(w3s + off) = hi;
-    *reinterpret_cast<float*>(w3s + BO * kH * 4 + off) = to_tf32(w - hi);
+    *reinterpret_cast<float*>(w3s + kmajor_off(q / kH, q % kH, 2 * BO)) = to_tf32(w - hi);
+    *reinterpret_cast<float*>(w3s + kmajor_off(BO + q / kH, q % kH, 2 * BO)) = hi;
   }
   for (int q = tid; q < kH * NB; q += kThreads) {
     const int h = q / NB, n = q % NB;
@@ -122,16 +123,18 @@ __global__ void __launch_bounds__(kThreads, 1)
   unsigned char* a_hi = sm + L.a + wg * 2 * kPlane;
   unsigned char* a_lo = a_hi + kPlane;
   const uint32_t a_hi_s = smem_u32(a_hi), a_lo_s = a_hi_s + kPlane;
-  const uint32_t w2_hi_s = smem_u32(w2s), w2_lo_s = w2_hi_s + kH * kH * 4;
-  const uint32_t w3_hi_s = smem_u32(w3s), w3_lo_s = w3_hi_s + BO * kH * 4;
-  const uint32_t col0 = tbase + wg * 128;                                   // this warpgroup's columns
+  const uint32_t w2_s = smem_u32(w2s), w3_s = smem_u32(w3s);
+  const uint32_t col0 = tbase + wg * 256;                                   // this warpgroup's columns
   const uint32_t tl = col0 + ((uint32_t)((warp & 3) * 32) << 16);          // + this warp's lane quarter
   volatile int* ab = &abort_[wg];
   uint32_t parity = 0;
 
-  // one MMA round: operand writes -> async proxy, sync the warpgroup, one thread issues D = A . B^T over
-  // K = 64 in 8 steps x 3 split terms, commits, and everyone waits for completion
-  auto round = [&](uint32_t dcol, uint32_t b_hi, uint32_t b_lo, uint32_t b_rows, uint32_t idesc) {
+  // one MMA round: operand writes -> async proxy, sync the warpgroup, one thread issues over K = 64 in 8 steps
+  //   [D_s | D_b] (=|+)= A_hi . [W_lo | W_hi],  D_s += A_lo . W_hi
+  // (D_s at dcol, D_b at dcol + R), commits, and everyone waits for completion
+  auto round = [&](uint32_t dcol, uint32_t w_s, uint32_t R) {
+    const uint32_t quad = 2 * R * 16;                                       // one 16-byte K quad of both halves
+    const uint32_t idesc2 = idesc_tf32(kRows, 2 * R), idesc1 = idesc_tf32(kRows, R);
     fence_proxy_async_smem();
     fence_before_sync();
     bar_sync(1 + wg, 2 * kRows);
@@ -141,11 +144,10 @@ __global__ void __launch_bounds__(kThreads, 1)
       for (int s = 0; s < kH / 8; s++) {
         const uint64_t ah = desc_kmajor(a_hi_s + s * 2 * kRows * 16, kRows * 16, 128);
         const uint64_t al = desc_kmajor(a_lo_s + s * 2 * kRows * 16, kRows * 16, 128);
-        const uint64_t bh = desc_kmajor(b_hi + s * 2 * b_rows * 16, b_rows * 16, 128);
-        const uint64_t bl = desc_kmajor(b_lo + s * 2 * b_rows * 16, b_rows * 16, 128);
-        mma_tf32(dcol, ah, bh, idesc, s > 0 ? 1u : 0u);
-        mma_tf32(dcol, ah, bl, idesc, 1u);
-        mma_tf32(dcol, al, bh, idesc, 1u);
+        const uint64_t bb = desc_kmajor(w_s + s * 2 * quad, quad, 128);             // [W_lo | W_hi], 2R rows
+        const uint64_t bh = desc_kmajor(w_s + s * 2 * quad + R * 16, quad, 128);    // W_hi, R rows
+        mma_tf32(dcol, ah, bb, idesc2, s > 0 ? 1u : 0u);
+        mma_tf32(dcol, al, bh, idesc1, 1u);
       }
       commit(&mbar[wg]);
     }
@@ -205,60 +207,68 @@ __global__ void __launch_bounds__(kThreads, 1)
       }
       store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), a[0], a[1], a[2], a[3]);
     }
-    round(col0, w2_hi_s, w2_lo_s, kH, idesc_tf32(kRows, kH));                // z2 -> columns [0, 64)
+    round(col0, w2_s, kH);                                                   // z2 -> columns [0, 128)
 #pragma unroll
     for (int hh = 0; hh < kHh; hh += 4)
       store_split4(a_hi, a_lo, kmajor_off(row, half * kHh + hh, kRows), da1[hh], da1[hh + 1], da1[hh + 2],
                    da1[hh + 3]);
-    round(col0 + 64, w2_hi_s, w2_lo_s, kH, idesc_tf32(kRows, kH));           // dz2 -> columns [64, 128)
+    round(col0 + 128, w2_s, kH);                                             // dz2 -> columns [128, 256)
 
     // ---- silu epilogue of layer 2: a2 -> operand planes, da2 kept in registers
     float da2[kHh];
 #pragma unroll
-    for (int cc = 0; cc < kHh; cc += 16) {
+    for (int cc = 0; cc < kHh; cc += 8) {
       const int c0 = half * kHh + cc;
-      float z[16], dz[16];
-      tmem_ld16(tl + c0, z);
-      tmem_ld16(tl + 64 + c0, dz);
+      float z[8], dz[8], ts[8], td[8];
+      tmem_ld8(tl + c0, z);
+      tmem_ld8(tl + 64 + c0, ts);
+      tmem_ld8(tl + 128 + c0, dz);
+      tmem_ld8(tl + 192 + c0, td);
       tmem_wait_ld();
-      float a[16];
+      float a[8];
 #pragma unroll
-      for (int j = 0; j < 16; j++) {
-        const float zz = z[j] + b2s[c0 + j];
+      for (int j = 0; j < 8; j++) {
+        const float zz = (z[j] + ts[j]) + b2s[c0 + j];
         const float sg = sigmoid_f(zz);
         a[j] = zz * sg;
-        da2[cc + j] = sg * (1.f + zz * (1.f - sg)) * dz[j];
+        da2[cc + j] = sg * (1.f + zz * (1.f - sg)) * (dz[j] + td[j]);
       }
 #pragma unroll
-      for (int q = 0; q < 16; q += 4)
+      for (int q = 0; q < 8; q += 4)
         store_split4(a_hi, a_lo, kmajor_off(row, c0 + q, kRows), a[q], a[q + 1], a[q + 2], a[q + 3]);
     }
-    round(col0, w3_hi_s, w3_lo_s, BO, idesc_tf32(kRows, BO));                // z3 -> columns [0, BO)
+    round(col0, w3_s, BO);                                                   // z3 -> columns [0, 2 BO)
 #pragma unroll
     for (int hh = 0; hh < kHh; hh += 4)
       store_split4(a_hi, a_lo, kmajor_off(row, half * kHh + hh, kRows), da2[hh], da2[hh + 1], da2[hh + 2],
                    da2[hh + 3]);
-    round(col0 + 32, w3_hi_s, w3_lo_s, BO, idesc_tf32(kRows, BO));           // dz3 -> columns [32, 32 + BO)
+    round(col0 + 64, w3_s, BO);                                              // dz3 -> columns [64, 64 + 2 BO)
 
-    // ---- output epilogue: 16-column groups split between the two halves (half 1 idle when BO = 16)
+    // ---- output epilogue: 16-column groups split between the two halves (half 1 idle when BO = 16), read
+    // 8 columns at a time
 #pragma unroll
     for (int c0 = 16 * half; c0 < BO; c0 += 32) {
-      float z[16], dz[16];
-      tmem_ld16(tl + c0, z);
-      tmem_ld16(tl + 32 + c0, dz);
-      tmem_wait_ld();
-      if (valid) {
 #pragma unroll
-        for (int q = 0; q < 16; q += 4) {
-          float v[4], d[4];
+      for (int c8 = c0; c8 < c0 + 16; c8 += 8) {
+        float z[8], zb[8], dz[8], dzb[8];
+        tmem_ld8(tl + c8, z);
+        tmem_ld8(tl + BO + c8, zb);
+        tmem_ld8(tl + 64 + c8, dz);
+        tmem_ld8(tl + 64 + BO + c8, dzb);
+        tmem_wait_ld();
+        if (valid) {
 #pragma unroll
-          for (int j = 0; j < 4; j++) {
-            v[j] = z[q + j] + b3s[c0 + q + j];
-            d[j] = dz[q + j] * env + v[j] * denv;
-            v[j] *= env;
+          for (int q = 0; q < 8; q += 4) {
+            float v[4], d[4];
+#pragma unroll
+            for (int j = 0; j < 4; j++) {
+              v[j] = (z[q + j] + zb[q + j]) + b3s[c8 + q + j];
+              d[j] = (dz[q + j] + dzb[q + j]) * env + v[j] * denv;
+              v[j] *= env;
+            }
+            *reinterpret_cast<float4*>(phi + e * BO + c8 + q) = make_float4(v[0], v[1], v[2], v[3]);
+            *reinterpret_cast<float4*>(dphidr + e * BO + c8 + q) = make_float4(d[0], d[1], d[2], d[3]);
           }
-          *reinterpret_cast<float4*>(phi + e * BO + c0 + q) = make_float4(v[0], v[1], v[2], v[3]);
-          *reinterpret_cast<float4*>(dphidr + e * BO + c0 + q) = make_float4(d[0], d[1], d[2], d[3]);
         }
       }
     }
