@@ -249,7 +249,7 @@ def run_ours(a):
     if not a.no_cpu:
         cpu, _, _ = time_cpu_oracle(a.config, budget_s=a.cpu_budget)
     out = {"metric": METRIC, "value": value, "unit": UNIT, "n_gpus": 1, "steps": a.steps, "warmup": a.warmup,
-           "ms_per_step": ms, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "ms_per_step": ms, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
            "dtype": "f32" if dtype == torch.float32 else "f64", "data": "synthetic (seeded geometry, seeded random-init weights)",
            "config": {"workload": f"cfg{a.config}: " + ("1,048,576-atom fcc 5-element alloy, C64, 2 passes, PME 256^3"
                                                          if a.config == 5 and not a.scale else
@@ -274,7 +274,7 @@ def run_reference(a):
     cpu, ts, n = time_cpu_oracle(a.config, steps=a.steps, warmup=a.warmup)
     med = statistics.median(ts)
     out = {"metric": METRIC, "value": n / med, "unit": UNIT, "n_gpus": a.gpus, "steps": a.steps, "warmup": a.warmup,
-           "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+           "ms_per_step": med * 1e3, "higher_is_better": True, "scaling": "strong", "vs_baseline": None,
            "dtype": "f64" if a.config == 1 else "f32", "data": "synthetic (seeded geometry, seeded random-init weights)",
            "impl": "reference", "config": {"workload": f"cfg{a.config} (bounded CPU sample: {cpu['sample']})"},
            "cpu_baseline": cpu, "e2e": {"value": n / med, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
