@@ -4,6 +4,7 @@ The local model is the CPU oracle, so this checks the multi-GPU logic without a 
 owned-atom energies, the all-reduced neutrality sums, the all-gathered global charges feeding real space and PME,
 and the all-reduced force gradient -- against the oracle evaluated on the whole periodic system in one process.
 """
+import datetime
 import math
 import os
 import socket
@@ -70,7 +71,8 @@ def _oracle_parts(P, cfg, g_local, cell):
 def _worker(rank, world, port, out):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
-    dist.init_process_group("gloo", rank=rank, world_size=world)
+    # a short timeout so that a rank left waiting for a failed peer ends with an error instead of hanging
+    dist.init_process_group("gloo", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120))
     try:
         from face_b200 import domain
         st = _system()
@@ -95,8 +97,15 @@ def _worker(rank, world, port, out):
         dist.all_reduce(et)
         if rank == 0:
             out.put((float(et[0]), (-g).numpy(), int(owned.sum()), int(gid.numel())))
+            out.close()
+            out.join_thread()                          # the result is in the pipe before this process ends
+        dist.barrier()                                 # both ranks are out of their last collective
     finally:
         dist.destroy_process_group()
+    # Success: leave without interpreter finalisation.  Teardown of gloo's threads and of the libraries' static
+    # state at exit occasionally aborted a worker (SIGABRT) after its result had been delivered; an error above
+    # still propagates and gives a non-zero exit code.
+    os._exit(0)
 
 
 def _free_port():
