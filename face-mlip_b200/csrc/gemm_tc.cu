@@ -25,6 +25,11 @@
 //                      partial of the chunk three behind is loaded from TMEM while the split runs and folded into
 //                      fp32 registers; a finished tile leaves through padded shared memory as coalesced
 //                      16-byte stores (bias and accumulate applied there).  No block-wide barrier per chunk.
+// Tile store: tiles of 64 or 128 columns leave by TMA (each warpgroup writes its rows' 32-column block into a
+// 128-byte-swizzled staging block, one thread issues a bulk tensor store, or a bulk tensor add when accumulating
+// into C, and the warpgroup moves on while the copy engine writes HBM); other widths store through padded shared
+// memory as coalesced 16-byte stores.  The asynchronous store keeps the compute warps' epilogue short for the
+// output-heavy adjoint maps (K = 64, N = 512), where it had been the longest step of each tile.
 // The tensor core accumulates in fp32 with truncation, so a long chain of MMAs into one accumulator drifts toward
 // zero; each K chunk therefore starts a fresh TMEM partial (four rotate) and the partials are summed in
 // registers with round-to-nearest (the truncating chain is 12 MMAs long whatever K is).
@@ -32,6 +37,8 @@
 // CTAs are persistent over (M tile, N tile) units (consecutive units share the A tile, so its re-reads hit L2).
 // Every mbarrier wait is bounded and parity-safe: no barrier is ever two phases ahead of a waiter.
 #include <cuda.h>
+
+#include <cstring>
 
 #include "common.cuh"
 #include "tc.cuh"
@@ -120,15 +127,36 @@ struct Cursor {
   }
 };
 
+// bulk tensor store / add of a 2D box from shared memory (async proxy), grouped per thread
+__device__ __forceinline__ void tma_store_2d(const CUtensorMap* map, int x, int y, const void* src) {
+  asm volatile("cp.async.bulk.tensor.2d.global.shared::cta.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void tma_add_2d(const CUtensorMap* map, int x, int y, const void* src) {
+  asm volatile("cp.reduce.async.bulk.tensor.2d.global.shared::cta.add.bulk_group [%0, {%1, %2}], [%3];" ::"l"(
+                   reinterpret_cast<uint64_t>(map)),
+               "r"(x), "r"(y), "r"(smem_u32(src))
+               : "memory");
+}
+__device__ __forceinline__ void bulk_commit() { asm volatile("cp.async.bulk.commit_group;" ::: "memory"); }
+// this thread's bulk groups have finished reading their shared-memory sources
+__device__ __forceinline__ void bulk_wait_read() { asm volatile("cp.async.bulk.wait_group.read 0;" ::: "memory"); }
+// this thread's bulk groups are complete (global writes performed)
+__device__ __forceinline__ void bulk_wait_all() { asm volatile("cp.async.bulk.wait_group 0;" ::: "memory"); }
+
 __device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(mbar)) : "memory");
 }
 
 template <int H16>
-__global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUtensorMap amap, GemmArgs g) {
+__global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUtensorMap amap,
+                                                     const __grid_constant__ CUtensorMap cmap, GemmArgs g) {
   constexpr int SA = Ring<H16>::SA, SW = Ring<H16>::SW;
   constexpr int Nt = 32 * H16;
   constexpr int HALF = Nt / 2;                                 // columns per compute warpgroup
+  constexpr bool kTmaOut = HALF % 32 == 0;                     // tile store by TMA (Nt = 64, 128)
   constexpr uint32_t wbytes = 2u * Nt * kKc * 4;               // W hi + lo of one chunk
   extern __shared__ unsigned char sm_raw[];
   unsigned char* sm = sm_raw + ((1024u - (smem_u32(sm_raw) & 1023u)) & 1023u);   // 1024-byte aligned
@@ -259,6 +287,37 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUt
         const int64_t row0 = dc.mt * kM;
         const int64_t gcb = (int64_t)dc.nt * Nt + wg * HALF;
         float* stg = stage_out + wg * (kStg / 4);
+        if constexpr (kTmaOut) {
+          // dense 128 x 32 block, 16-byte quad q of row r at sw128(r, q) (the TMA box layout, 128-byte swizzle)
+          unsigned char* sb = reinterpret_cast<unsigned char*>(stg);
+#pragma unroll
+          for (int cb = 0; cb < HALF; cb += 32) {
+            if (row == 0) bulk_wait_read();                      // the previous store has read the staging
+            bar_sync(1 + wg, kM);
+            const int64_t gc0 = gcb + cb;
+#pragma unroll
+            for (int q = 0; q < 8; q++) {
+              float4 o = make_float4(acc[cb + 4 * q], acc[cb + 4 * q + 1], acc[cb + 4 * q + 2], acc[cb + 4 * q + 3]);
+              if (g.bias) {
+                const int64_t gc = gc0 + 4 * q;                  // N % 4 == 0: a quad is all in or all out
+                if (gc < g.N) {
+                  o.x += g.bias[gc];
+                  o.y += g.bias[gc + 1];
+                  o.z += g.bias[gc + 2];
+                  o.w += g.bias[gc + 3];
+                }
+              }
+              *reinterpret_cast<float4*>(sb + sw128(row, q)) = o;
+            }
+            fence_proxy_async_smem();                            // staging writes -> async proxy
+            bar_sync(1 + wg, kM);
+            if (row == 0) {
+              if (g.beta) tma_add_2d(&cmap, (int)gc0, (int)row0, sb);
+              else tma_store_2d(&cmap, (int)gc0, (int)row0, sb);
+              bulk_commit();
+            }
+          }
+        } else {
 #pragma unroll
         for (int cb = 0; cb < HALF; cb += 32) {
           const int w = HALF - cb < 32 ? HALF - cb : 32;        // 16 or 32
@@ -293,6 +352,7 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUt
             }
           }
         }
+        }
 #pragma unroll
         for (int c = 0; c < HALF; c++) acc[c] = 0.f;
       }
@@ -326,6 +386,7 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUt
         if (!drain_start(t)) break;
         drain_finish();
       }
+    if (kTmaOut && row == 0) bulk_wait_all();                  // tile stores performed before the CTA exits
   }
   fence_before_sync();
   __syncthreads();
@@ -380,7 +441,7 @@ EncodeTiledFn encode_fn() {
 }
 
 template <int H16>
-int launch_gemm(const CUtensorMap& amap, const GemmArgs& g, void* stream) {
+int launch_gemm(const CUtensorMap& amap, const CUtensorMap& cmap, const GemmArgs& g, void* stream) {
   constexpr int Nt = 32 * H16;
   constexpr int SA = Ring<H16>::SA, SW = Ring<H16>::SW;
   const size_t smem =
@@ -389,7 +450,7 @@ int launch_gemm(const CUtensorMap& amap, const GemmArgs& g, void* stream) {
   cudaFuncSetAttribute(gemm_tc_k<H16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t units = ((g.M + kM - 1) / kM) * g.n_tiles;
   const int grid = (int)std::min<int64_t>(units, sm_count());
-  gemm_tc_k<H16><<<grid, kThr, smem, as_stream(stream)>>>(amap, g);
+  gemm_tc_k<H16><<<grid, kThr, smem, as_stream(stream)>>>(amap, cmap, g);
   return launch_status("facek_gemm_tc");
 }
 
@@ -465,10 +526,23 @@ extern "C" int facek_gemm_tc(const float* A, int64_t M, int64_t K, int64_t lda, 
   uint32_t cols = 32;
   while (cols < (uint32_t)(kNB * g.Nt)) cols <<= 1;             // kNB chunk partials
   g.tmem_cols = cols;
+  // C as a TMA destination for the 64- and 128-column tiles (box 32 columns x 128 rows, 128-byte swizzle; TMA
+  // clips the rows >= M and columns >= N of the last tiles); unused by the other widths
+  CUtensorMap cmap;
+  std::memset(&cmap, 0, sizeof(cmap));
+  if (g.Nt % 64 == 0) {
+    const cuuint64_t cdims[2] = {(cuuint64_t)N, (cuuint64_t)M};
+    const cuuint64_t cstrides[1] = {(cuuint64_t)ldc * 4};
+    const cuuint32_t cbox[2] = {32, (cuuint32_t)kM};
+    const CUresult cc = enc(&cmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, C, cdims, cstrides, cbox, estr,
+                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    FACEK_CHECK_ARG(cc == CUDA_SUCCESS, "facek_gemm_tc: output tensor map encoding failed (%d)", (int)cc);
+  }
   switch (g.Nt / 32) {
-    case 1: return launch_gemm<1>(amap, g, stream);
-    case 2: return launch_gemm<2>(amap, g, stream);
-    case 3: return launch_gemm<3>(amap, g, stream);
-    default: return launch_gemm<4>(amap, g, stream);
+    case 1: return launch_gemm<1>(amap, cmap, g, stream);
+    case 2: return launch_gemm<2>(amap, cmap, g, stream);
+    case 3: return launch_gemm<3>(amap, cmap, g, stream);
+    default: return launch_gemm<4>(amap, cmap, g, stream);
   }
 }

@@ -88,3 +88,27 @@ def test_tcmatmul_autograd_two_terms():
     assert _rel(g1, G.double() @ W1.double().t()) < 2e-6
     assert _rel(g2, G.double() @ W2.double().t()) < 2e-6
     assert _status() == 0
+
+
+@pytest.mark.parametrize("M,K,N", [(1001, 64, 100), (300, 64, 512), (129, 512, 64), (5000, 96, 128)])
+def test_gemm_tma_store_bias_and_accumulate(M, K, N):
+    """64- and 128-column tiles leave by TMA (bulk store; bulk add when accumulating): ragged M and N tails are
+    clipped by the copy engine, bias is added before the store, and C += A.W + b goes through the bulk add."""
+    from face_b200.ops import Dense, _gemm
+    g = torch.Generator(device=DEV).manual_seed(M * 3 + N)
+    big = torch.full((M + 3, N + 8), float("nan"), device=DEV)
+    A = torch.randn(M, K, device=DEV, generator=g)
+    W = torch.randn(K, N, device=DEV, generator=g) * K ** -0.5
+    b = torch.randn(N, device=DEV, generator=g)
+    d = Dense(W, b)
+    C = big[:M, :N]                                                 # ldc = N + 8; neighbours stay NaN
+    C0 = torch.randn(M, N, device=DEV, generator=g)
+    C.copy_(C0)
+    _gemm(A, d.img, K, N, d.b, C, 1)
+    ref = C0.double() + A.double() @ W.double() + b.double()
+    assert _rel(C, ref) < max(4 * _rel(C0 + A @ W + b, ref), 2e-6)
+    assert torch.isnan(big[:M, N:]).all() and torch.isnan(big[M:]).all()    # nothing written outside C
+    _gemm(A, d.img, K, N, d.b, C, 0)
+    ref = A.double() @ W.double() + b.double()
+    assert _rel(C, ref) < max(4 * _rel(A @ W + b, ref), 2e-6)
+    assert _status() == 0
