@@ -417,11 +417,11 @@ __global__ void gemm_pack_k(const float* __restrict__ W, int64_t K, int64_t N, i
 }
 
 int pick_nt(int64_t N) {
-  // N tile: a multiple of 32 (epilogue halves of 16-column loads) up to 128 (four TMEM partials and three ring
-  // stages fit); wider N splits into equal tiles
+  // N tile: 32 or 64 for narrow maps, else 128 (the most that four TMEM partials and the W ring hold).  An MMA costs
+  // the same for any N up to 128, so a wider tile never costs tensor time, and the 64- and 128-column tiles store
+  // by TMA (columns past N are clipped by the copy engine)
   const int64_t n32 = (N + 31) / 32;
-  const int64_t tiles = (n32 + 3) / 4;
-  return (int)((n32 + tiles - 1) / tiles) * 32;
+  return n32 <= 2 ? (int)n32 * 32 : 128;
 }
 
 typedef CUresult (*EncodeTiledFn)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
