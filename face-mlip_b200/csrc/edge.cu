@@ -283,6 +283,42 @@ __global__ void edge_msg_k(const T* __restrict__ Y, const int32_t* __restrict__ 
   }
 }
 
+// fp32, K = 32, nc <= 10: eight lanes per edge (a float4 of k each), four edges per warp; the component loop is
+// unrolled so that all of an edge's table rows are requested at once, and no index division is needed
+__global__ void __launch_bounds__(256) edge_msg32_k(const float* __restrict__ Y, const int32_t* __restrict__ ei,
+                                                    const int32_t* __restrict__ ej, const float4* __restrict__ TJ,
+                                                    const float4* __restrict__ TI, int nc, int64_t N,
+                                                    float4* __restrict__ msg, int64_t E) {
+  const int64_t NK4 = N * 8;                                   // one component plane, in float4
+  const int sub = threadIdx.x & 7;
+  for (int64_t e = (blockIdx.x * (int64_t)blockDim.x + threadIdx.x) >> 3; e < E;
+       e += ((int64_t)gridDim.x * blockDim.x) >> 3) {
+    const float4* tj = TJ + (int64_t)ej[e] * 8 + sub;
+    const float4* ti = TI ? TI + (int64_t)ei[e] * 8 + sub : nullptr;
+    const float* y = Y + e * NX;
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int c = 0; c < 10; c++) {
+      if (c < nc) {
+        float4 t = __ldg(tj + c * NK4);
+        if (ti) {
+          const float4 u = __ldg(ti + c * NK4);
+          t.x += u.x;
+          t.y += u.y;
+          t.z += u.z;
+          t.w += u.w;
+        }
+        const float yc = __ldg(y + c);
+        s.x += yc * t.x;
+        s.y += yc * t.y;
+        s.z += yc * t.z;
+        s.w += yc * t.w;
+      }
+    }
+    msg[e * 8 + sub] = s;
+  }
+}
+
 // dY[e, c<nc] (+)= sum_k dmsg[e,k] (TJ[ej,c,k] + TI[ei,c,k]); one warp per edge
 template <typename T>
 __global__ void edge_msg_bwd_dy_k(const int32_t* __restrict__ ei, const int32_t* __restrict__ ej,
@@ -853,6 +889,12 @@ template <typename T>
 int msg_fwd(const void* Y, const int32_t* ei, const int32_t* ej, const void* TJ, const void* TI, int nc, int K,
             void* msg, int64_t N, int64_t E, void* stream) {
   if (E == 0) return FACEK_OK;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(TJ) | reinterpret_cast<uintptr_t>(TI) | reinterpret_cast<uintptr_t>(msg);
+  if (std::is_same<T, float>::value && K == 32 && nc <= 10 && (al & 15) == 0) {
+    edge_msg32_k<<<elem_grid(E * 8, 256), 256, 0, as_stream(stream)>>>((const float*)Y, ei, ej, (const float4*)TJ,
+                                                                        (const float4*)TI, nc, N, (float4*)msg, E);
+    return launch_status("facek_edge_msg_fwd");
+  }
   const int64_t EK = E * K;
   edge_msg_k<T><<<elem_grid(EK, 256), 256, 0, as_stream(stream)>>>((const T*)Y, ei, ej, (const T*)TJ, (const T*)TI,
                                                                     nc, K, N, (T*)msg, EK);

@@ -202,28 +202,33 @@ def test_radial_fp64(small_graph, spline):
     assert rel(torch.autograd.grad((phi * G_).sum(), pos)[0], torch.autograd.grad((phi2 * G_).sum(), pos2)[0]) < 1e-10
 
 
+@pytest.mark.parametrize("dt", [torch.float64, torch.float32])
 @pytest.mark.parametrize("nc", [1, 10])
-def test_edge_msg_fp64(small_graph, nc):
+def test_edge_msg_fp64(small_graph, nc, dt):
+    """EdgeMsg (fp32 K = 32 runs the eight-lanes-per-edge kernel) against the torch statement of the message."""
     from face_b200.ops import EdgeMsg, EdgeSym, EdgeVec
     g = small_graph
     N = g["pos"].shape[0]
     K = 32
     torch.manual_seed(5)
-    pos = g["pos"].clone().requires_grad_(True)
-    Y = EdgeSym.apply(EdgeVec.apply(pos, g))
-    TJ = torch.randn(nc, N, K, device=DEV, dtype=torch.float64, requires_grad=True)
-    TI = torch.randn(nc, N, K, device=DEV, dtype=torch.float64, requires_grad=True) if nc > 1 else None
+    pos = g["pos"].clone().to(dt).requires_grad_(True)
+    gg = dict(g, shift=g["shift"].to(dt))
+    Y = EdgeSym.apply(EdgeVec.apply(pos, gg))
+    TJ = torch.randn(nc, N, K, device=DEV, dtype=dt, requires_grad=True)
+    TI = torch.randn(nc, N, K, device=DEV, dtype=dt, requires_grad=True) if nc > 1 else None
+    tol_f, tol_b = (1e-14, 1e-12) if dt == torch.float64 else (2e-6, 2e-5)
+    g = gg
     m = EdgeMsg.apply(Y, TJ, TI, g)
     ei, ej = g["ei"].long(), g["ej"].long()
     tab = (TJ[:, ej] + (TI[:, ei] if TI is not None else 0)).transpose(0, 1)            # (E, nc, K)
     m2 = (Y[:, :nc, None] * tab).sum(1)
-    assert rel(m, m2) < 1e-14
+    assert rel(m, m2) < tol_f
     G = torch.randn_like(m)
     wrt = [pos, TJ] + ([TI] if TI is not None else [])
     g1 = torch.autograd.grad((m * G).sum(), wrt, retain_graph=True)
     g2 = torch.autograd.grad((m2 * G).sum(), wrt)
     for u, v in zip(g1, g2):
-        assert rel(u, v) < 1e-12
+        assert rel(u, v) < tol_b
 
 
 def test_density_csr_fp64(small_graph):
