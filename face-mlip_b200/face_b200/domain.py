@@ -241,10 +241,71 @@ class DistributedModel:
         return et[0], -g
 
 
+# --------------------------------------------------------------------------------------------- structure sharding
+def shard_structures(natoms, world):
+    """Independent structures (a molecule batch) to ranks, balanced by atom count.
+
+    Largest structure first, each to the rank with the fewest atoms so far (ties to the lower rank), so every rank's
+    share is within one structure of the mean.  Returns one ascending index array per rank (possibly empty when there
+    are fewer structures than ranks)."""
+    natoms = np.asarray(natoms, np.int64)
+    load = np.zeros(world, np.int64)
+    own = [[] for _ in range(world)]
+    for s in np.argsort(-natoms, kind="stable"):
+        r = int(np.argmin(load))
+        own[r].append(int(s))
+        load[r] += natoms[s]
+    return [np.array(sorted(o), np.int64) for o in own]
+
+
+class ShardedBatch:
+    """Energies and forces of a batch of independent non-periodic structures on `world` GPUs (this process = one rank).
+
+    face-mlip evaluates a batch in one `FACE.forward` and sums atom energies per structure with `index_add` over
+    `batch` (face/model.py:680-695); structures never interact, so each rank evaluates only its own share
+    (`shard_structures`) and the data path has no collective.  One all-reduce of the zero-filled per-structure energy
+    vector (each entry written by exactly one rank) gives every rank the batch's energies; forces stay on the rank
+    that owns the structure, in the order of `self.ids`.
+
+    `evaluate(structures) -> (energy (n,), forces (atoms, 3))` evaluates a list of structures on this rank; the
+    default builds the engine's CSR graph and runs `model`."""
+
+    def __init__(self, model, structures, rank, world, device, dtype=torch.float32, group=None, evaluate=None):
+        self.rank, self.world, self.dev, self.dtype, self.group = rank, world, device, dtype, group
+        self.nstr = len(structures)
+        self.ids = shard_structures([len(s.numbers) for s in structures], world)[rank]
+        self.local = [structures[i] for i in self.ids]
+        self.n_local_atoms = int(sum(len(s.numbers) for s in self.local))
+        self.model = model
+        self.evaluate = evaluate or self._engine
+        self.graph = None
+        if evaluate is None and self.local:
+            from .neighbors import build_graph
+            self.graph = build_graph(self.local, model.rc, device=device, dtype=dtype)
+
+    def _engine(self, structures):
+        out = self.model(dict(self.graph, pos=self.graph["pos"].detach().clone()))
+        return out["energy"].detach(), out["forces"]
+
+    def energy_forces(self):
+        """Returns (energies of all structures (nstr,), forces of this rank's atoms (n_local_atoms, 3))."""
+        E = torch.zeros(self.nstr, dtype=self.dtype, device=self.dev)
+        if self.local:
+            e, F = self.evaluate(self.local)
+            E[torch.as_tensor(self.ids, device=self.dev)] = e.to(self.dtype)
+        else:
+            F = torch.zeros(0, 3, dtype=self.dtype, device=self.dev)
+        if self.world > 1:
+            dist.all_reduce(E, group=self.group)
+        return E, F
+
+
 # --------------------------------------------------------------------------------------------- benchmark
 def bench_multi(a):
     """bench.py --gpus N under torchrun: the 1,048,576-atom alloy decomposed over N GPUs (strong scaling)."""
     import datetime
+    if a.config == 3:
+        return bench_sharded(a)
     sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
     import bench as B
     rank = int(os.environ.get("RANK", 0))
@@ -342,6 +403,84 @@ def bench_multi(a):
                                 "bytes_per_launch": bytes_launch,
                                 "peak_source": "measured" if "hbm_gbs" in pk else "fallback"},
                    "gpu_launches": int(launches)}
+            print(json.dumps(out), flush=True)
+    finally:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def bench_sharded(a):
+    """bench.py --config 3 --gpus N under torchrun: the 512-molecule batch sharded by structure (weak per-structure
+    work, fixed batch: every rank evaluates its share, one all-reduce of the per-structure energies per step)."""
+    import datetime
+    sys.path.insert(0, os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__)))))
+    import bench as B
+    from . import _lib
+    rank = int(os.environ.get("RANK", 0))
+    world = int(os.environ.get("WORLD_SIZE", 1))
+    local = int(os.environ.get("LOCAL_RANK", rank))
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=300), device_id=dev)
+    try:
+        dtype = torch.float32
+        structs, spec, pme = B.workload(3, scale=a.scale)
+        model = B.make_model(spec, pme, dev, dtype)
+        natoms = sum(len(s.numbers) for s in structs)
+        sb = ShardedBatch(model, structs, rank, world, dev, dtype)
+        for _ in range(a.warmup):
+            sb.energy_forces()
+        torch.cuda.synchronize()
+        dist.barrier()
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        _lib.CALLS.clear()
+        _lib.COUNTING = True
+        with B.Clocks(local) as clk:
+            torch.cuda.synchronize()
+            dist.barrier()
+            e0.record()
+            for _ in range(a.steps):
+                E, F = sb.energy_forces()
+            e1.record()
+            torch.cuda.synchronize()
+            dist.barrier()
+        _lib.COUNTING = False
+        launches = torch.tensor([_lib.launches()], device=dev)
+        dist.all_reduce(launches)
+        ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
+        dist.all_reduce(ms, op=dist.ReduceOp.MAX)
+        ms = float(ms)
+        # e2e: this rank's positions from pinned host memory each step, forces back to the host
+        e2e = None
+        if not a.no_e2e and sb.graph is not None:
+            host = sb.graph["pos"].detach().cpu().pin_memory()
+            ke = max(1, a.steps // 2)
+            torch.cuda.synchronize()
+            dist.barrier()
+            t0 = time.perf_counter()
+            for _ in range(ke):
+                sb.graph["pos"] = host.to(dev, non_blocking=True)
+                E, F = sb.energy_forces()
+                Fh = F.cpu()
+            torch.cuda.synchronize()
+            dist.barrier()
+            dt = torch.tensor([(time.perf_counter() - t0) / ke], device=dev)
+            dist.all_reduce(dt, op=dist.ReduceOp.MAX)
+            e2e = {"value": natoms / float(dt), "unit": B.UNIT, "h2d_bytes_per_step": sb.n_local_atoms * 3 * 4,
+                   "d2h_bytes_per_step": sb.n_local_atoms * 3 * 4, "ms_per_step": float(dt) * 1e3,
+                   "note": "per rank, max over ranks"}
+        counts = torch.tensor([sb.n_local_atoms], device=dev)
+        allc = [torch.zeros_like(counts) for _ in range(world)]
+        dist.all_gather(allc, counts)
+        if rank == 0:
+            out = {"metric": B.METRIC, "value": natoms * 1e3 / ms, "unit": B.UNIT, "n_gpus": world, "steps": a.steps,
+                   "warmup": a.warmup, "ms_per_step": ms, "higher_is_better": True, "scaling": "strong",
+                   "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded geometry, seeded random-init weights)",
+                   "config": {"workload": f"cfg3: {len(structs)} molecules, {natoms} atoms, sharded by structure",
+                              "atoms": natoms, "atoms_per_rank": [int(c) for c in allc],
+                              "l2": "batch smaller than L2 (cfg3 is a small workload)",
+                              "parallelism": f"structure sharding over {world} ranks, NCCL all-reduce of energies"},
+                   "e2e": e2e, "energy_sum": float(E.sum()), "clocks": clk.summary(), "gpu_launches": int(launches)}
             print(json.dumps(out), flush=True)
     finally:
         dist.barrier()
