@@ -17,7 +17,7 @@ namespace facek {
 namespace {
 
 constexpr int NX = 20;
-constexpr int FWD_TILE = 32;
+constexpr int FWD_TILE = 48;                 // one tile per row at the alloys' ~44 neighbours
 
 // D / G addressing: element (i, x, q) at base[r(x)] + (x - off[r(x)]) * sX + i * sN + q, r(x) the rank of x
 // (x in [0,1) [1,4) [4,10) [10,20)).  Reference layout (N,20,BK): one buffer, sN = 20 BK, sX = BK.
@@ -270,6 +270,9 @@ int launch_fwd(const void* phi, const void* msg, const void* Y, Planes<T*> D, in
   const int threads = (B / TB) * (K / TK);
   const int threads_r = ceil_div(threads, 32) * 32;
   const size_t smem = 2 * sizeof(T) * FWD_TILE * (NX + B + K);
+  FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_density_fwd: edge tiles %zu B exceed shared memory", smem);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(dens_fwd_k<T, TB, TK>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int grid = grid_for(N, 6);
   dens_fwd_k<T, TB, TK><<<grid, threads_r, smem, as_stream(stream)>>>((const T*)phi, (const T*)msg, (const T*)Y,
                                                                      D, N, rows, B, K);
@@ -312,7 +315,8 @@ int launch_bwd(const void* phi, const void* msg, const void* Y, Planes<const T*>
 // Backward, L lanes per edge (fp32, B = 16, K = 32).  A 48 L-thread CTA takes one row (atom) at a time: it stages
 // the row's G (20 x 512 fp32, 40 KB) in shared memory with cp.async, then each edge's L lanes walk the 320 rows
 // (x, b) of G, each lane reading its 1/L of the row's k range as 16-byte broadcasts:
-//   t = sum_k msg[k] g[k] (shuffles join the parts)  ->  dphi[b] += t Y[x],  dY[x] += t phi[b]
+//   t = sum_k msg[k] g[k] (each lane its part)  ->  dphi[b] += t Y[x],  dY[x] += t phi[b]  (parts joined by shuffles
+//   once per x for dY and once per edge for dphi)
 //   dmsg[k] += Y[x] phi[b] g[k]
 // msg and dmsg parts of the edge in registers.  48 edges per round keeps ~90% of the lanes busy at the alloys'
 // ~44 neighbours; five CTAs share an SM, so one CTA's staging overlaps the others' work.  The five G tiles leave
@@ -387,17 +391,23 @@ __global__ void __launch_bounds__(48 * L, L >= 4 ? 4 : 5)
           float t0_ = 0.f, t1 = 0.f;
 #pragma unroll
           for (int k = 0; k < KH; k += 2) ffma2(t0_, t1, m[k], m[k + 1], g[k], g[k + 1]);
-          float t = t0_ + t1;
-#pragma unroll
-          for (int o = 1; o < L; o <<= 1) t += __shfl_xor_sync(pair_mask, t, o);
+          // this lane's part of t: dp and dY are linear in t, so the lanes' parts are joined once per x (dY)
+          // and once per edge (dphi) instead of once per (x, b)
+          const float t = t0_ + t1;
           dp[b] += t * yx;
           dyx += t * p[b];
           const float w = yx * p[b];
 #pragma unroll
           for (int k = 0; k < KH; k += 2) ffma2(dm[k], dm[k + 1], w, w, g[k], g[k + 1]);
         }
+#pragma unroll
+        for (int o = 1; o < L; o <<= 1) dyx += __shfl_xor_sync(pair_mask, dyx, o);
         if (half == 0) dY[e * NX + x] = dyx;
       }
+#pragma unroll
+      for (int b = 0; b < BB; b++)
+#pragma unroll
+        for (int o = 1; o < L; o <<= 1) dp[b] += __shfl_xor_sync(pair_mask, dp[b], o);
       if (half == 0) {
 #pragma unroll
         for (int b = 0; b < BB; b += 4)

@@ -1,5 +1,6 @@
 """Worker for tests/test_gpu_multi.py: fp64 alloy (cfg5 model, 15x15x15 cells, 54 A box) decomposed over the torchrun world;
-rank 0 compares energy and forces with the single-GPU engine and writes the differences to argv[1]."""
+rank 0 compares energy and forces with the single-GPU engine and writes the differences to argv[1].  Then a 16-molecule
+batch (cfg3 model, fp64) sharded by structure, against the whole batch on one GPU."""
 import datetime
 import json
 import os
@@ -16,7 +17,7 @@ sys.path.insert(0, os.path.join(ROOT, "face-mlip_b200"))
 
 def main():
     from face_b200 import systems
-    from face_b200.domain import DistributedModel
+    from face_b200.domain import DistributedModel, ShardedBatch
     from face_b200.model import FACE
     from face_b200.neighbors import build_graph
     rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
@@ -36,10 +37,28 @@ def main():
         dm = DistributedModel(m, st, rank, world, dev, torch.float64)
         pos = torch.as_tensor(st.positions, dtype=torch.float64, device=dev)
         E, F = dm.energy_forces(pos)
+        # molecule batch sharded by structure (cfg3 model) against the whole batch on one GPU
+        spec3 = dict(systems.model_kwargs(3))
+        mb3 = spec3.pop("max_body")
+        m3 = FACE(**spec3)
+        m3.set_max_body(mb3)
+        m3 = m3.seed_(1).to(dev, torch.float64)
+        mols = systems.molecule_batch(16, seed=3)
+        sb = ShardedBatch(m3, mols, rank, world, dev, torch.float64)
+        Es, Fs = sb.energy_forces()
+        off = np.concatenate([[0], np.cumsum([len(s.numbers) for s in mols])])
+        o3 = m3(build_graph(mols, m3.rc, device=dev, dtype=torch.float64))
+        Fr = torch.cat([o3["forces"][off[i]:off[i + 1]] for i in sb.ids]) if len(sb.ids) else Fs
+        dEs = torch.tensor([float((Es - o3["energy"]).abs().max() / o3["energy"].abs().max()),
+                            float((Fs - Fr).abs().max()) if len(sb.ids) else 0.0, float(len(sb.ids))], device=dev)
+        allm = [torch.zeros_like(dEs) for _ in range(world)]
+        dist.all_gather(allm, dEs)
         if rank == 0:
             o = m(build_graph([st], 5.0, device=dev, dtype=torch.float64))
             res = {"dE_rel": abs(float(E) - float(o["energy"][0])) / abs(float(o["energy"][0])),
-                   "dF": float((F - o["forces"]).abs().max()), "E": float(E)}
+                   "dF": float((F - o["forces"]).abs().max()), "E": float(E),
+                   "shard_dE_rel": max(float(t[0]) for t in allm), "shard_dF": max(float(t[1]) for t in allm),
+                   "shard_counts": [int(t[2]) for t in allm]}
             open(sys.argv[1], "w").write(json.dumps(res))
     finally:
         dist.barrier()
