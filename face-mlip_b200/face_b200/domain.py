@@ -94,7 +94,7 @@ def rank_energy(pos_global, gid, img, owned, local_model, coulomb=None, world=1,
     local_model(pos_local) -> (e_at, h): per-atom model energies and final features of the local atoms.
     coulomb (optional): dict with
         head(h) -> (chi, J);  real_rows(pos_local, q_local) -> e_row;  pme(pos_global, q_global) -> scalar;
-        gp, volume, charge (total charge Q), n_global, gid_owned_all (global ids of every rank's owned atoms in
+        optionally pme_slab(pos_owned, q_owned) -> this rank's share of the reciprocal energy (SlabPME);  gp, volume, charge (total charge Q), n_global, gid_owned_all (global ids of every rank's owned atoms in
         all-gather order, padded with -1), max_owned.
     Sum over ranks = the system's energy."""
     from torch.distributed.nn import functional as dnn
@@ -127,13 +127,73 @@ def rank_energy(pos_global, gid, img, owned, local_model, coulomb=None, world=1,
     q_loc = q_g[gid]
     e_row = coulomb["real_rows"](pos_local, q_loc)
     e_real = (e_row * w).sum()
-    e_recip = coulomb["pme"](pos_global, q_g)
+    if coulomb.get("pme_slab") is not None:          # this rank's k-space share of the mesh-distributed PME
+        e_recip_share = coulomb["pme_slab"](pos_global[gid[oi]], q_o)
+    else:                                            # full mesh on every rank, counted 1/world
+        e_recip_share = coulomb["pme"](pos_global, q_g) / world
     gp = coulomb["gp"]
     self_o = -(q_o * q_o).sum() / (math.sqrt(math.pi) * gp)
     qsum = allr(q_o.sum())
     bg = -0.5 * math.pi * gp ** 2 / coulomb["volume"] * qsum * qsum
-    e_es = KE * (e_real + e_recip / world + self_o + bg / world)
+    e_es = KE * (e_real + e_recip_share + self_o + bg / world)
     return e + (chi_o * q_o + 0.5 * J_o * q_o * q_o).sum() + e_es
+
+
+class SlabPME:
+    """Smooth-PME reciprocal energy (face/electrostatics.py:54-77) with the mesh distributed over the ranks in slabs.
+
+    Each rank spreads its own atoms' charges onto a full-size mesh (`spread(pos, q) -> (n0*n1*n2,)`, differentiable);
+    a reduce-scatter along x leaves rank r the summed x-planes [r*n0/W, (r+1)*n0/W) (the spreading stencil's overlap
+    into neighbouring slabs is summed by the same collective).  A 2-D FFT over (y, z) of the slab, an all-to-all that
+    trades x-slabs for y-slabs, and a 1-D FFT along x give the rank the full structure factor S(k) for its k_y
+    block; its energy share is 1/(2V) sum G(k) |b(k)|^2 |S(k)|^2 over that block, and the shares sum to the energy.
+    All collectives are the differentiable ones of torch.distributed.nn, so forces and charge gradients flow back
+    through the transposes to the spreading adjoint (the gather).  n0 and n1 must be multiples of the world size."""
+
+    def __init__(self, cell64, gp, mesh, rank, world, spread, dtype, device, group=None):
+        n0, n1, n2 = (int(n) for n in mesh)
+        if n0 % world or n1 % world:
+            raise ValueError(f"PME mesh {mesh} not divisible into {world} slabs along x and y")
+        self.mesh, self.rank, self.world, self.group, self.spread = (n0, n1, n2), rank, world, group, spread
+        cell = np.asarray(cell64, np.float64)
+        inv = np.linalg.inv(cell)
+        self.volume = abs(float(np.linalg.det(cell)))
+        nb = n1 // world
+        m = [np.fft.fftfreq(n, 1.0 / n) for n in (n0, n1, n2)]
+        m[1] = m[1][rank * nb:(rank + 1) * nb]
+        mg = np.stack(np.meshgrid(*m, indexing="ij"), -1)
+        k = 2 * math.pi * mg @ inv.T
+        k2 = (k * k).sum(-1)
+        G = np.where(k2 > 1e-12, 4 * math.pi / np.maximum(k2, 1e-12) * np.exp(-gp ** 2 * k2 / 4), 0.0)
+        bm = [_bspline_modulus2(n) for n in (n0, n1, n2)]
+        Bm = bm[0][:, None, None] * bm[1][None, rank * nb:(rank + 1) * nb, None] * bm[2][None, None, :]
+        self.gfac = torch.as_tensor(0.5 / self.volume * G * Bm, dtype=dtype, device=device)
+
+    def __call__(self, pos, q):
+        from torch.distributed.nn import functional as dnn
+        n0, n1, n2 = self.mesh
+        W = self.world
+        grid = self.spread(pos, q).view(n0, n1, n2)
+        if W > 1:
+            slab = dnn.reduce_scatter(grid.new_empty(n0 // W, n1, n2), list(grid.chunk(W, 0)), group=self.group)
+        else:
+            slab = grid
+        A = torch.fft.fft2(slab, dim=(1, 2))                                  # (n0/W, n1, n2), this x-slab
+        if W > 1:
+            send = [c.contiguous() for c in torch.view_as_real(A).chunk(W, 1)]  # y-blocks of the x-slab
+            recv = dnn.all_to_all([torch.empty_like(send[0]) for _ in range(W)], send, group=self.group)
+            A = torch.view_as_complex(torch.cat(list(recv), 0).contiguous())  # (n0, n1/W, n2), this y-block
+        S = torch.fft.fft(A, dim=0)
+        return (self.gfac * (S.real * S.real + S.imag * S.imag)).sum()
+
+
+def _bspline_modulus2(n):
+    """|b(m)|^-2 of the order-4 B-spline interpolation (Essmann et al. 1995; face/electrostatics.py:44-51)."""
+    m = np.arange(n, dtype=np.float64)
+    w = np.array([1 / 6, 4 / 6, 1 / 6])
+    ang = 2 * math.pi * m[:, None] * np.arange(3)[None] / n
+    den = (w * np.cos(ang)).sum(-1) ** 2 + (w * np.sin(ang)).sum(-1) ** 2
+    return 1.0 / np.maximum(den, 1e-10)
 
 
 def owned_ids_all(gid, owned, world, group=None):
@@ -189,8 +249,13 @@ class EngineParts:
 class DistributedModel:
     """Energy and forces of one periodic structure on `world` GPUs (this process = one rank)."""
 
-    def __init__(self, model, structure, rank, world, device, dtype=torch.float32, group=None):
+    def __init__(self, model, structure, rank, world, device, dtype=torch.float32, group=None, pme="replicated"):
+        """pme: "replicated" (the full mesh on every rank, counted 1/world) or "slab" (SlabPME: the mesh in x-slabs,
+        FFT transposed by an all-to-all; needs mesh dimensions 0 and 1 divisible by world)."""
         from .neighbors import build_graph
+        if pme not in ("replicated", "slab"):
+            raise ValueError(f"pme={pme!r}")
+        self.pme_mode, self._slab = pme, None
         self.model, self.rank, self.world, self.dev, self.dtype, self.group = model, rank, world, device, dtype, group
         cell = np.asarray(structure.cell, np.float64)
         if np.abs(cell - np.diag(np.diag(cell))).max() > 0:
@@ -225,6 +290,14 @@ class DistributedModel:
             self.coulomb = {"head": self.parts.head, "real_rows": self.parts.real_rows, "pme": self.parts.pme,
                             "gp": float(tm.gp), "volume": float(abs(np.linalg.det(self.cell64))), "charge": self.Q,
                             "n_global": self.n_global, "gid_owned_all": ids, "max_owned": mx}
+            if self.pme_mode == "slab":
+                if self._slab is None:                  # the cell and mesh are fixed: Green's factors built once
+                    from . import ops
+                    cell64, mesh_t = self.cell64, tuple(mesh)
+                    self._slab = SlabPME(cell64, float(tm.gp), mesh_t, self.rank, self.world,
+                                         lambda p, q: ops.SpreadMesh.apply(p, q.contiguous(), cell64, mesh_t),
+                                         self.dtype, self.dev, self.group)
+                self.coulomb["pme_slab"] = self._slab
 
     def energy_forces(self, pos_global):
         """pos_global: (N,3) model-dtype device tensor of all atoms (same on every rank).  Returns (E_total, forces)
@@ -322,7 +395,7 @@ def bench_multi(a):
         model = B.make_model(spec, pme, dev, dtype)
         st = structs[0]
         natoms = len(st.numbers)
-        dm = DistributedModel(model, st, rank, world, dev, dtype)
+        dm = DistributedModel(model, st, rank, world, dev, dtype, pme=getattr(a, "pme", "replicated"))
         pos = torch.as_tensor(st.positions, dtype=dtype, device=dev)
         n_local = int(dm.gid.numel())
         for _ in range(a.warmup):
@@ -395,7 +468,7 @@ def bench_multi(a):
                    "config": {"workload": f"cfg{a.config}: {natoms}-atom periodic system, spatial decomposition",
                               "atoms": natoms, "bricks": list(dm.grid), "halo_A": dm.halo,
                               "local_atoms_per_rank": [int(c) for c in allc],
-                              "l2": "inputs larger than L2", "parallelism": f"spatial {dm.grid} over NCCL"},
+                              "l2": "inputs larger than L2", "parallelism": f"spatial {dm.grid} over NCCL", "pme": dm.pme_mode},
                    "e2e": e2e, "energy": float(E), "clocks": clk.summary(),
                    "roofline": {"kernel": "facek_density_xm_fwd (dens_fwd_k), rank 0 local system", "bound": "hbm",
                                 "achieved": achieved, "peak": hbm, "unit": "GB/s",

@@ -390,6 +390,34 @@ class PMERecip(torch.autograd.Function):
         return dpos, dq, None, None, None
 
 
+class SpreadMesh(torch.autograd.Function):
+    """Order-4 B-spline charge spreading onto the full PME mesh (the spreading step of face/electrostatics.py:54-77)
+    as a differentiable op: forward facek_pme_spread, adjoint facek_pme_gather of the mesh gradient (dq and dpos).
+    Used by the slab-distributed PME, where the mesh leaves this op through collectives and FFTs."""
+
+    @staticmethod
+    def forward(ctx, pos, q, cell64, mesh):
+        pos, q = pos.detach().contiguous(), q.detach().contiguous()
+        n0, n1, n2 = mesh
+        inv = np.linalg.inv(cell64)
+        grid = torch.zeros(n0 * n1 * n2, dtype=pos.dtype, device=pos.device)
+        _lib.call("facek_pme_spread", _tag(pos), _p(pos), _p(q), pos.shape[0], _lib.doubles(inv.reshape(-1)), n0,
+                  n1, n2, _p(grid), _lib.stream())
+        ctx.save_for_backward(pos, q)
+        ctx.inv, ctx.mesh = inv, mesh
+        return grid
+
+    @staticmethod
+    def backward(ctx, g):
+        pos, q = ctx.saved_tensors
+        n0, n1, n2 = ctx.mesh
+        dq = torch.empty_like(q)
+        dpos = torch.empty_like(pos)
+        _lib.call("facek_pme_gather", _tag(pos), _p(pos), _p(q), pos.shape[0], _lib.doubles(ctx.inv.reshape(-1)), n0,
+                  n1, n2, _p(g.contiguous()), 1.0, _p(dq), _p(dpos), _lib.stream())
+        return dpos, dq, None, None
+
+
 # ============================================================================================ channel GEMMs
 class Dense:
     """A constant (K, N) fp32 weight packed for the tensor-core GEMM (facek_gemm_tc): the split image of W for

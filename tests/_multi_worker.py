@@ -1,5 +1,5 @@
 """Worker for tests/test_gpu_multi.py: fp64 alloy (cfg5 model, 15x15x15 cells, 54 A box) decomposed over the torchrun world;
-rank 0 compares energy and forces with the single-GPU engine and writes the differences to argv[1].  Then a 16-molecule
+rank 0 compares energy and forces with the single-GPU engine and writes the differences to argv[1], with the PME mesh on every rank and in x-slabs.  Then a 16-molecule
 batch (cfg3 model, fp64) sharded by structure, against the whole batch on one GPU."""
 import datetime
 import json
@@ -37,6 +37,8 @@ def main():
         dm = DistributedModel(m, st, rank, world, dev, torch.float64)
         pos = torch.as_tensor(st.positions, dtype=torch.float64, device=dev)
         E, F = dm.energy_forces(pos)
+        dms = DistributedModel(m, st, rank, world, dev, torch.float64, pme="slab")   # mesh in x-slabs
+        Esl, Fsl = dms.energy_forces(pos)
         # molecule batch sharded by structure (cfg3 model) against the whole batch on one GPU
         spec3 = dict(systems.model_kwargs(3))
         mb3 = spec3.pop("max_body")
@@ -57,6 +59,8 @@ def main():
             o = m(build_graph([st], 5.0, device=dev, dtype=torch.float64))
             res = {"dE_rel": abs(float(E) - float(o["energy"][0])) / abs(float(o["energy"][0])),
                    "dF": float((F - o["forces"]).abs().max()), "E": float(E),
+                   "slab_dE_rel": abs(float(Esl) - float(o["energy"][0])) / abs(float(o["energy"][0])),
+                   "slab_dF": float((Fsl - o["forces"]).abs().max()),
                    "shard_dE_rel": max(float(t[0]) for t in allm), "shard_dF": max(float(t[1]) for t in allm),
                    "shard_counts": [int(t[2]) for t in allm]}
             open(sys.argv[1], "w").write(json.dumps(res))

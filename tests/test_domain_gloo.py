@@ -68,7 +68,24 @@ def _oracle_parts(P, cfg, g_local, cell):
     return local_model, head, real_rows, pme
 
 
-def _worker(rank, world, port, out):
+def _oracle_spread(cell, mesh):
+    """Differentiable order-4 B-spline spreading onto the full mesh (the first half of face_ref.pme_recip_energy)."""
+    inv = torch.linalg.inv(torch.as_tensor(cell, dtype=torch.float64))
+    n = list(mesh)
+
+    def spread(pos, q):
+        u = (pos @ inv) * pos.new_tensor(n)
+        base = torch.floor(u)
+        W = face_ref.bspline4(u - base)
+        ib = base.long()
+        idx = [(ib[:, d, None] - torch.arange(4)) % n[d] for d in range(3)]
+        w = q[:, None, None, None] * W[:, 0, :, None, None] * W[:, 1, None, :, None] * W[:, 2, None, None, :]
+        flat = (idx[0][:, :, None, None] * n[1] + idx[1][:, None, :, None]) * n[2] + idx[2][:, None, None, :]
+        return torch.zeros(n[0] * n[1] * n[2], dtype=pos.dtype).index_add(0, flat.reshape(-1), w.reshape(-1))
+    return spread
+
+
+def _worker(rank, world, port, out, mode="replicated"):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     # a short timeout so that a rank left waiting for a failed peer ends with an error instead of hanging
@@ -89,6 +106,9 @@ def _worker(rank, world, port, out):
         coul = {"head": head, "real_rows": real_rows, "pme": pme, "gp": PME["gp"],
                 "volume": float(abs(np.linalg.det(st.cell))), "charge": 0.0, "n_global": len(st.numbers),
                 "gid_owned_all": ids, "max_owned": mx}
+        if mode == "slab":
+            coul["pme_slab"] = domain.SlabPME(st.cell, PME["gp"], PME["mesh"], rank, world,
+                                              _oracle_spread(st.cell, PME["mesh"]), torch.float64, "cpu")
         pos = pos_g.clone().requires_grad_(True)
         e = domain.rank_energy(pos, gid, img, owned, local_model, coul, world)
         (g,) = torch.autograd.grad(e, pos)
@@ -116,7 +136,10 @@ def _free_port():
     return p
 
 
-def test_two_rank_decomposition_matches_single_system():
+@pytest.mark.parametrize("mode", ["replicated", "slab"])
+def test_two_rank_decomposition_matches_single_system(mode):
+    """mode "replicated": the PME mesh on every rank; "slab": the mesh in x-slabs with the FFT transposed by an
+    all-to-all (SlabPME)."""
     st = _system()
     cfg = dict(SPEC)
     g = nlist.padded_graph([st], cfg["rc"])
@@ -124,7 +147,7 @@ def test_two_rank_decomposition_matches_single_system():
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
     for p in procs:
         p.start()
     E, F, n_owned, n_local = q.get(timeout=600)

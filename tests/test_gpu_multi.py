@@ -24,6 +24,7 @@ def test_two_gpu_decomposition_matches_single_gpu(tmp_path):
     assert r.returncode == 0, r.stdout[-3000:] + r.stderr[-3000:]
     res = json.loads(out.read_text())
     assert res["dE_rel"] <= 1e-10 and res["dF"] <= 1e-9, res
+    assert res["slab_dE_rel"] <= 1e-10 and res["slab_dF"] <= 1e-9, res          # slab-distributed PME
     # structure sharding: every molecule on exactly one rank, energies and forces as evaluated in one batch
     assert sum(res["shard_counts"]) == 16 and min(res["shard_counts"]) > 0, res
     assert res["shard_dE_rel"] <= 1e-10 and res["shard_dF"] <= 1e-9, res
