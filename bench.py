@@ -254,7 +254,8 @@ def run_ours(a):
            "config": {"workload": f"cfg{a.config}: " + ("1,048,576-atom fcc 5-element alloy, C64, 2 passes, PME 256^3"
                                                          if a.config == 5 and not a.scale else
                                                          f"BASELINE configuration {a.config}, scale {a.scale}"),
-                      "atoms": natoms, "edges": E, "l2": "inputs larger than L2 (edge tensors of several GB)",
+                      "atoms": natoms, "edges": E, "l2": ("inputs larger than L2 (edge tensors of several GB)" if E * 4 * 20 > 126e6 else
+                             "small workload: edge tensors fit in L2, not flushed between steps"),
                       "parallelism": "single GPU"},
            "e2e": e2e,
            "roofline": {"kernel": "facek_density_xm_fwd (dens_fwd_k)", "bound": "hbm", "achieved": achieved, "peak": hbm,

@@ -371,15 +371,35 @@ __global__ void edge_msg_bwd_tables_k(const T* __restrict__ Y, const T* __restri
     T sj[10], si[10];
 #pragma unroll
     for (int c = 0; c < 10; c++) { sj[c] = 0; si[c] = 0; }
-    for (int e = row_ptr[a]; e < row_ptr[a + 1]; e++) {
+    const int e1 = row_ptr[a + 1];
+#pragma unroll 2
+    for (int e = row_ptr[a]; e < e1; e++) {
       const int64_t r = rev[e];
       const T gr = dmsg[r * K + k];
       const T ge = dmsg[(int64_t)e * K + k];
+      T yr[10], ye[10];
+      if constexpr (sizeof(T) == 4) {          // Y rows are 80 B (16-byte aligned): the first ten as 4 + 4 + 2
+        const float4* r4 = reinterpret_cast<const float4*>(Y + r * NX);
+        const float4* e4 = reinterpret_cast<const float4*>(Y + (int64_t)e * NX);
+        const float4 ra = __ldg(r4), rb = __ldg(r4 + 1), ea = __ldg(e4), eb = __ldg(e4 + 1);
+        const float2 rc = __ldg(reinterpret_cast<const float2*>(r4 + 2));
+        const float2 ec = __ldg(reinterpret_cast<const float2*>(e4 + 2));
+        yr[0] = ra.x; yr[1] = ra.y; yr[2] = ra.z; yr[3] = ra.w; yr[4] = rb.x; yr[5] = rb.y; yr[6] = rb.z;
+        yr[7] = rb.w; yr[8] = rc.x; yr[9] = rc.y;
+        ye[0] = ea.x; ye[1] = ea.y; ye[2] = ea.z; ye[3] = ea.w; ye[4] = eb.x; ye[5] = eb.y; ye[6] = eb.z;
+        ye[7] = eb.w; ye[8] = ec.x; ye[9] = ec.y;
+      } else {
+#pragma unroll
+        for (int c = 0; c < 10; c++) {
+          yr[c] = Y[r * NX + c];
+          ye[c] = Y[(int64_t)e * NX + c];
+        }
+      }
 #pragma unroll
       for (int c = 0; c < 10; c++)
         if (c < nc) {
-          sj[c] += Y[r * NX + c] * gr;
-          si[c] += Y[(int64_t)e * NX + c] * ge;
+          sj[c] += yr[c] * gr;
+          si[c] += ye[c] * ge;
         }
     }
 #pragma unroll
@@ -929,6 +949,8 @@ int msg_bwd(const void* Y, const int32_t* ei, const int32_t* ej, const void* TJ,
   }
   if (N > 0) {
     const int64_t NK = N * K;
+    FACEK_CHECK_ARG(E == 0 || (reinterpret_cast<uintptr_t>(Y) & 15) == 0,
+                    "facek_edge_msg_bwd: Y must be 16-byte aligned (rows are read as 16-byte vectors)");
     edge_msg_bwd_tables_k<T><<<elem_grid(NK, 128), 128, 0, as_stream(stream)>>>((const T*)Y, (const T*)dmsg, row_ptr,
                                                                                  rev, nc, K, (T*)dTJ, (T*)dTI, NK);
     return launch_status("facek_edge_msg_bwd(tables)");
