@@ -9,9 +9,11 @@ random-init weights.  A step is one energy + forces evaluation of the whole syst
 face-mlip tools/bench.py:57-60; neighbour list built once outside the device-timed region, as there).
 
 One JSON line on rank 0 with: value (atoms/s over all GPUs), e2e (the public calculator call with host positions in
-pinned memory, neighbour list, forces back to the host), roofline of the density kernel (algorithmic bytes per
-launch / CUDA-event launch time vs the measured HBM copy bandwidth), cpu_baseline (the CPU oracle on a bounded
-sub-box on the host cores), clocks sampled during the timed region, gpu_launches.
+pinned memory, neighbour list, forces back to the host), roofline of the dominant kernel by time per step
+(algorithmic bytes and FLOPs per launch / CUDA-event launch time, against the measured HBM copy bandwidth and the
+FP32 SIMT peak; the density forward, density adjoint and channel GEMM each have a row, see face_b200.perf),
+cpu_baseline (the CPU oracle on a bounded sub-box on the host cores), clocks sampled during the timed region,
+gpu_launches.
 
 --impl reference: face-mlip's own algorithm (the CPU restatement in oracle/, the reference being a PyTorch package
 that cannot run here) on the host cores, same metric and configuration, each step a bounded sub-box sample.
@@ -38,13 +40,6 @@ import torch  # noqa: E402
 
 METRIC = "energy+force atoms/sec"
 UNIT = "atoms/s"
-
-
-def peaks():
-    try:
-        return json.load(open(os.path.join(ROOT, "MEASURED_PEAKS.json")))
-    except Exception:
-        return {}
 
 
 # --------------------------------------------------------------------------------------------- workload
@@ -166,7 +161,7 @@ class Clocks:
 
 # --------------------------------------------------------------------------------------------- GPU arm
 def run_ours(a):
-    from face_b200 import _lib
+    from face_b200 import _lib, perf
     from face_b200.calculator import FACECalculator
     from face_b200.neighbors import build_graph
     rank = int(os.environ.get("RANK", 0))
@@ -198,6 +193,7 @@ def run_ours(a):
     # device-timed region: K steps, inputs resident in HBM (well above the 126 MB L2: edge tensors are GBs)
     for name in _lib.SIGNATURES:
         _lib.TIMED[name] = []
+    perf.start()
     _lib.CALLS.clear()
     _lib.COUNTING = True
     e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -212,22 +208,12 @@ def run_ours(a):
     launches = _lib.launches()
     ms = e0.elapsed_time(e1) / a.steps
     kernel_ms = {k[6:]: round(sum(s.elapsed_time(t) for s, t in v) / a.steps, 3) for k, v in _lib.TIMED.items() if v}
-    dens_ms = [s.elapsed_time(t) for s, t in _lib.TIMED["facek_density_xm_fwd"]]
-    _lib.TIMED.clear()
     value = natoms * a.steps / (e0.elapsed_time(e1) / 1e3)
-    # density-kernel roofline: algorithmic bytes of one launch (phi, msg, Y per edge read; D per atom written)
-    B, K = spec["B"], spec["K"]
+    # roofline of the dominant kernels: algorithmic bytes and FLOPs per launch (face_b200.perf) over CUDA-event times
     esz = 4 if dtype == torch.float32 else 8
-    N = natoms
-    bytes_launch = esz * E * (B + K + 20) + esz * N * 20 * B * K + 4 * (N + 1)
-    t_launch = statistics.mean(dens_ms) / 1e3
-    pk = peaks()
-    hbm = pk.get("hbm_gbs", 6650.0)
-    achieved = bytes_launch / t_launch / 1e9
-    traffic = None
-    tf = os.path.join(ROOT, "profiles", "density_fwd_traffic.json")
-    if os.path.exists(tf):
-        traffic = json.load(open(tf)).get("bytes_per_launch_full_size")
+    rows, pk = perf.collect(E, natoms, spec["B"], spec["K"], esz, a.steps, ROOT,
+                            traffic=perf.traffic_full_size(ROOT, E, natoms))
+    _lib.TIMED.clear()
     # e2e: the public calculator call (host positions -> pinned -> device, neighbour list, forces back to host)
     e2e = None
     if not a.no_e2e:
@@ -258,10 +244,7 @@ def run_ours(a):
                              "small workload: edge tensors fit in L2, not flushed between steps"),
                       "parallelism": "single GPU"},
            "e2e": e2e,
-           "roofline": {"kernel": "facek_density_xm_fwd (dens_fwd_k)", "bound": "hbm", "achieved": achieved, "peak": hbm,
-                        "unit": "GB/s", "frac": achieved / hbm, "traffic": traffic,
-                        "bytes_per_launch": bytes_launch, "launch_ms": t_launch * 1e3,
-                        "peak_source": "measured" if "hbm_gbs" in pk else "fallback"},
+           "roofline": perf.headline(rows, pk),
            "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
            "kernel_ms_per_step": kernel_ms}
     if rank == 0:

@@ -11,8 +11,6 @@
 // along each lattice plane normal; each atom scans (2ns+1)^3 cells, cell images giving the shift S.  Cell
 // contents are sorted by atom index, the per-row output is sorted by key, so the result is deterministic.
 // Non-periodic batches: all pairs inside each structure (molecules of tens of atoms).
-#include <mutex>
-
 #include "common.cuh"
 
 namespace facek {
@@ -232,6 +230,9 @@ __global__ void __launch_bounds__(128) cell_rows_k(const double* __restrict__ po
     }
     if (!FILL) {
       deg[i] = cnt;
+      // rows longer than MAXDEG are rejected before any row offsets are used: the fill pass cannot sort them, and
+      // with every row at most MAXDEG long the int32 prefix sum stays below 2^31 for up to 2^22 rows
+      if (cnt > MAXDEG) atomicExch(w.flag, 1);
       continue;
     }
     // sort the row by (j, S) and write shift vectors
@@ -365,28 +366,18 @@ constexpr int64_t NOALLOC_INTS = 3 * NOALLOC_MAX_CELLS + 1 + 5 * NOALLOC_MAX_ATO
 
 static __device__ __align__(256) int g_nlist_scratch[NOALLOC_INTS];     // about 7.1 MB per device
 
-// Device address of the scratch array for the current device: g_nlist_scratch named in host code is only a
-// host-side stand-in, so the address is looked up once per device with that device current.
+// Device address of the scratch array on the current device.  g_nlist_scratch named in host code is only a
+// host-side stand-in, so the address is looked up with cudaGetSymbolAddress, with the caller's device current, on
+// every call: a cached address would go stale if the host application reset the device or its primary context,
+// and the lookup costs little next to the call's two stream synchronisations.
 int noalloc_scratch(int** out) {
-  static std::mutex mu;
-  static int* addr[128] = {nullptr};
-  int dev = 0;
-  cudaError_t e = cudaGetDevice(&dev);
-  if (e != cudaSuccess || dev < 0 || dev >= 128) {
-    set_error("facek_nlist_cell_build_noalloc: cudaGetDevice failed (%s)", cudaGetErrorString(e));
+  void* p = nullptr;
+  const cudaError_t e = cudaGetSymbolAddress(&p, g_nlist_scratch);
+  if (e != cudaSuccess || !p) {
+    set_error("facek_nlist_cell_build_noalloc: cudaGetSymbolAddress failed (%s)", cudaGetErrorString(e));
     return FACEK_ELAUNCH;
   }
-  std::lock_guard<std::mutex> lock(mu);
-  if (!addr[dev]) {
-    void* p = nullptr;
-    e = cudaGetSymbolAddress(&p, g_nlist_scratch);
-    if (e != cudaSuccess || !p) {
-      set_error("facek_nlist_cell_build_noalloc: cudaGetSymbolAddress failed (%s)", cudaGetErrorString(e));
-      return FACEK_ELAUNCH;
-    }
-    addr[dev] = static_cast<int*>(p);
-  }
-  *out = addr[dev];
+  *out = static_cast<int*>(p);
   return FACEK_OK;
 }
 
@@ -419,9 +410,20 @@ int build_noalloc(const double* pos, int64_t N, const double* cell, double rc, i
   scan_k<<<1, 1024, 0, s>>>(deg, row_ptr, N);
   st = launch_status("facek_nlist_cell_build_noalloc(count)");
   if (st) return st;
-  int total = 0;
+  int total = 0, too_long = 0;
   cudaMemcpyAsync(&total, row_ptr + N, sizeof(int), cudaMemcpyDeviceToHost, s);
+  cudaMemcpyAsync(&too_long, w.flag, sizeof(int), cudaMemcpyDeviceToHost, s);
   if (cudaStreamSynchronize(s) != cudaSuccess) return launch_status("facek_nlist_cell_build_noalloc(sync)");
+  if (too_long) {
+    *n_edges = -1;
+    set_error("facek_nlist_cell_build_noalloc: a row has more than %d neighbours", MAXDEG);
+    return FACEK_EUNSUPPORTED;
+  }
+  if (total < 0) {      // unreachable with rows of at most MAXDEG and N <= NOALLOC_MAX_ATOMS; kept as a guard
+    *n_edges = -1;
+    set_error("facek_nlist_cell_build_noalloc: edge count overflow");
+    return FACEK_EUNSUPPORTED;
+  }
   *n_edges = total;
   if (total > max_edges) {
     set_error("facek_nlist_cell_build_noalloc: %d edges exceed the output capacity max_edges=%lld", total,

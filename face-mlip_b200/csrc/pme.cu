@@ -5,6 +5,8 @@
 //            conv = G B F * (n0 n1 n2 / V) so that irfftn(conv) = dE/dQ on the mesh
 //   gather : dE/dq_i = sum W phi, dE/dpos_i = q_i sum (dW/du) (du/dpos) phi (autograd of the reference, :60-68)
 //   real   : e_i = 1/2 sum_{e in row i} q_i q_j (erf(r/gamma) - erf(r/gp)) / r and its adjoint
+#include <limits>
+
 #include "common.cuh"
 
 namespace facek {
@@ -161,13 +163,14 @@ __device__ __forceinline__ void gauss_kernel(T r, T gamma, T gp, T& K, T& dK) {
 
 template <typename T>
 __global__ void real_fwd_k(const T* __restrict__ vec, const int32_t* __restrict__ row_ptr,
-                           const int32_t* __restrict__ ej, const T* __restrict__ q, T gamma, T gp, int64_t N,
+                           const int32_t* __restrict__ ej, const T* __restrict__ q, T gamma, T gp, T rcut, int64_t N,
                            T* __restrict__ e_row) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < N; i += (int64_t)gridDim.x * blockDim.x) {
     T s = 0;
     for (int e = row_ptr[i]; e < row_ptr[i + 1]; e++) {
       const T vx = vec[(int64_t)e * 3], vy = vec[(int64_t)e * 3 + 1], vz = vec[(int64_t)e * 3 + 2];
       const T r = sqrt(vx * vx + vy * vy + vz * vz);
+      if (r >= rcut) continue;                        // skin edges of a reused neighbour list
       T K, dK;
       gauss_kernel(r, gamma, gp, K, dK);
       s += q[ej[e]] * K;
@@ -180,7 +183,7 @@ __global__ void real_fwd_k(const T* __restrict__ vec, const int32_t* __restrict_
 // dq_i = sum_{e in row i} (g_i + g_j)/2 q_j K(r);  dvec[e] (+)= g_i q_i q_j K'(r) u / 2
 template <typename T>
 __global__ void real_bwd_k(const T* __restrict__ vec, const int32_t* __restrict__ row_ptr,
-                           const int32_t* __restrict__ ej, const T* __restrict__ q, T gamma, T gp,
+                           const int32_t* __restrict__ ej, const T* __restrict__ q, T gamma, T gp, T rcut,
                            const T* __restrict__ g_row, int64_t N, T* __restrict__ dvec, int acc, T* __restrict__ dq) {
   for (int64_t i = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; i < N; i += (int64_t)gridDim.x * blockDim.x) {
     T s = 0;
@@ -188,8 +191,8 @@ __global__ void real_bwd_k(const T* __restrict__ vec, const int32_t* __restrict_
     for (int e = row_ptr[i]; e < row_ptr[i + 1]; e++) {
       const T vx = vec[(int64_t)e * 3], vy = vec[(int64_t)e * 3 + 1], vz = vec[(int64_t)e * 3 + 2];
       const T r = sqrt(vx * vx + vy * vy + vz * vz);
-      T K, dK;
-      gauss_kernel(r, gamma, gp, K, dK);
+      T K = 0, dK = 0;
+      if (r < rcut) gauss_kernel(r, gamma, gp, K, dK);   // beyond the cut the edge contributes zero
       const int j = ej[e];
       const T qj = q[j];
       s += T(0.5) * (gi + g_row[j]) * qj * K;
@@ -202,6 +205,12 @@ __global__ void real_bwd_k(const T* __restrict__ vec, const int32_t* __restrict_
     }
     dq[i] = s;
   }
+}
+
+// real-space cut: r_cut <= 0 keeps every edge of the list (the reference's behaviour: the pair list is the model's)
+template <typename T>
+T cut_value(double rcut) {
+  return rcut > 0 ? (T)rcut : std::numeric_limits<T>::infinity();
 }
 
 Mesh make_mesh(const double* inv, int n0, int n1, int n2) {
@@ -240,18 +249,19 @@ int gather(const void* pos, const void* q, int64_t N, const double* inv, int n0,
 }
 template <typename T>
 int real_fwd(const void* vec, const int32_t* row_ptr, const int32_t* ej, const void* q, double gamma, double gp,
-             int64_t N, void* e_row, void* stream) {
+             double rcut, int64_t N, void* e_row, void* stream) {
   if (N == 0) return FACEK_OK;
   real_fwd_k<T><<<ew_grid(N, 128), 128, 0, as_stream(stream)>>>((const T*)vec, row_ptr, ej, (const T*)q, (T)gamma,
-                                                                (T)gp, N, (T*)e_row);
+                                                                (T)gp, cut_value<T>(rcut), N, (T*)e_row);
   return launch_status("facek_coulomb_real_fwd");
 }
 template <typename T>
 int real_bwd(const void* vec, const int32_t* row_ptr, const int32_t* ej, const void* q, double gamma, double gp,
-             const void* g, int64_t N, void* dvec, int acc, void* dq, void* stream) {
+             double rcut, const void* g, int64_t N, void* dvec, int acc, void* dq, void* stream) {
   if (N == 0) return FACEK_OK;
   real_bwd_k<T><<<ew_grid(N, 128), 128, 0, as_stream(stream)>>>((const T*)vec, row_ptr, ej, (const T*)q, (T)gamma,
-                                                                (T)gp, (const T*)g, N, (T*)dvec, acc, (T*)dq);
+                                                                (T)gp, cut_value<T>(rcut), (const T*)g, N, (T*)dvec,
+                                                                acc, (T*)dq);
   return launch_status("facek_coulomb_real_bwd");
 }
 
@@ -279,15 +289,17 @@ extern "C" int facek_pme_gather(int dtype, const void* pos, const void* q, int64
   return FACEK_DISPATCH(dtype, gather, pos, q, N, inv, n0, n1, n2, potential, scale, dq, dpos, stream);
 }
 extern "C" int facek_coulomb_real_fwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej,
-                                      const void* q, double gamma, double gp, int64_t N, void* e_row, void* stream) {
+                                      const void* q, double gamma, double gp, double r_cut, int64_t N, void* e_row,
+                                      void* stream) {
   FACEK_CHECK_ARG(N >= 0 && gamma > 0 && gp > 0 && (N == 0 || (vec && row_ptr && ej && q && e_row)),
                   "facek_coulomb_real_fwd: bad arguments");
-  return FACEK_DISPATCH(dtype, real_fwd, vec, row_ptr, ej, q, gamma, gp, N, e_row, stream);
+  return FACEK_DISPATCH(dtype, real_fwd, vec, row_ptr, ej, q, gamma, gp, r_cut, N, e_row, stream);
 }
 extern "C" int facek_coulomb_real_bwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej,
-                                      const void* q, double gamma, double gp, const void* g_row, int64_t N,
-                                      void* dvec, int32_t accumulate, void* dq, void* stream) {
+                                      const void* q, double gamma, double gp, double r_cut, const void* g_row,
+                                      int64_t N, void* dvec, int32_t accumulate, void* dq, void* stream) {
   FACEK_CHECK_ARG(N >= 0 && gamma > 0 && gp > 0 && (N == 0 || (vec && row_ptr && ej && q && g_row && dvec && dq)),
                   "facek_coulomb_real_bwd: bad arguments");
-  return FACEK_DISPATCH(dtype, real_bwd, vec, row_ptr, ej, q, gamma, gp, g_row, N, dvec, accumulate, dq, stream);
+  return FACEK_DISPATCH(dtype, real_bwd, vec, row_ptr, ej, q, gamma, gp, r_cut, g_row, N, dvec, accumulate, dq,
+                        stream);
 }

@@ -60,8 +60,8 @@ SIGNATURES = {
     "facek_pme_spread": [I32, P, P, I64, PD, I32, I32, I32, P, P],
     "facek_pme_green": [I32, P, I32, I32, I32, PD, D, D, P, P, P, P],
     "facek_pme_gather": [I32, P, P, I64, PD, I32, I32, I32, P, D, P, P, P],
-    "facek_coulomb_real_fwd": [I32, P, P, P, P, D, D, I64, P, P],
-    "facek_coulomb_real_bwd": [I32, P, P, P, P, D, D, P, I64, P, I32, P, P],
+    "facek_coulomb_real_fwd": [I32, P, P, P, P, D, D, D, I64, P, P],
+    "facek_coulomb_real_bwd": [I32, P, P, P, P, D, D, D, P, I64, P, I32, P, P],
 }
 
 _lib = None
@@ -72,6 +72,7 @@ LAUNCHES_PER_CALL = {"facek_nlist_cell_count": 5, "facek_edge_msg_bwd": 2, "face
 CALLS = {}            # name -> number of calls since reset (only while COUNTING)
 COUNTING = False
 TIMED = {}            # name -> list of (start, end) CUDA events, recorded around each call while enabled
+ARGS = {}             # name -> list of argument tuples of the timed calls (for per-call byte/FLOP accounting)
 
 
 def launches():
@@ -106,6 +107,8 @@ def call(name, *args):
         rc = getattr(lib(), name)(*args)
         e1.record()
         ev.append((e0, e1))
+        if name in ARGS:
+            ARGS[name].append(args)
     else:
         rc = getattr(lib(), name)(*args)
     if rc != 0:

@@ -10,7 +10,7 @@ import numpy as np
 import torch
 
 from .model import FACE
-from .neighbors import build_graph
+from .neighbors import _as_struct, build_graph
 
 try:                                                   # pragma: no cover - depends on the environment
     from ase.calculators.calculator import Calculator, all_changes
@@ -65,9 +65,18 @@ def load_face(path, device="cuda"):
 
 
 class FACECalculator(Calculator):
+    """Energy and forces of one atoms object (face/calculator.py:35-55).
+
+    `fused` is accepted for the reference's signature and ignored: the engine has only its CUDA path.
+    `skin` (Angstrom, default 0 = the reference's behaviour, a fresh neighbour list every call) keeps the neighbour
+    list of pairs closer than rc + skin across calls while no atom has moved more than skin/2 since it was built
+    (and species, cell and periodicity are unchanged), as MD drivers do (face/neighbors.py:7 builds such lists).
+    The model's envelope is zero beyond rc and the Coulomb real-space sum is cut at rc, so a reused list gives the
+    same energies and forces as a fresh one.  The reuse test costs one device-side max and one scalar read."""
     implemented_properties = ["energy", "forces"]
 
-    def __init__(self, path=None, device="cuda", fused=True, e_shift=0.0, model=None, dtype=torch.float32, **kw):
+    def __init__(self, path=None, device="cuda", fused=True, e_shift=0.0, model=None, dtype=torch.float32, skin=0.0,
+                 **kw):
         super().__init__(**kw)
         if model is None:
             model, ck = load_face(path, device)
@@ -75,12 +84,35 @@ class FACECalculator(Calculator):
         self.model = model.to(device=device, dtype=dtype)
         self.device, self.dtype = device, dtype
         self.e_shift = e_shift
+        self.skin = float(skin)
+        self._graph, self._key, self._stage = None, None, None
+        self.rebuilds = 0
+
+    def _positions(self, pos):
+        """Host positions -> device float64 through a pinned staging buffer."""
+        if self._stage is None or self._stage.shape != pos.shape:
+            self._stage = torch.empty(pos.shape, dtype=torch.float64, pin_memory=True)
+        self._stage.numpy()[:] = pos
+        return self._stage.to(self.device, non_blocking=True)
+
+    def graph(self, at):
+        """The neighbour graph for `at`: rebuilt, or (skin > 0) the previous one with the new positions."""
+        pos, Z, cell, pbc, q = _as_struct(at)
+        key = (Z.tobytes(), cell.tobytes(), pbc, q)
+        if self.skin > 0 and self._graph is not None and key == self._key:
+            p64 = self._positions(pos)
+            g = self._graph
+            if 2.0 * float((p64 - g["pos64"]).norm(dim=1).max()) < self.skin:
+                return dict(g, pos=p64.to(self.dtype))
+        self._graph = build_graph([at], self.model.rc, device=self.device, dtype=self.dtype, skin=self.skin)
+        self._key = key
+        self.rebuilds += 1
+        return self._graph
 
     def calculate(self, atoms=None, properties=("energy",), system_changes=all_changes):
         super().calculate(atoms, properties, system_changes)
         at = self.atoms if atoms is None else atoms
-        g = build_graph([at], self.model.rc, device=self.device, dtype=self.dtype)
-        o = self.model(g)
+        o = self.model(self.graph(at))
         self.results["energy"] = float(o["energy"].item()) + self.e_shift
         self.results["forces"] = o["forces"].detach().double().cpu().numpy()
 

@@ -243,7 +243,9 @@ class EngineParts:
 
     def pme(self, pos_global, q_global):
         c = self.P["coulomb"]
-        return self.ops.PMERecip.apply(pos_global, q_global.contiguous(), self.cell64, c["gp"], tuple(self.pme_mesh))
+        cell = np.asarray(self.cell64, np.float64)
+        return self.ops.PMERecip.apply(pos_global, q_global.contiguous(), np.linalg.inv(cell),
+                                       abs(float(np.linalg.det(cell))), c["gp"], tuple(self.pme_mesh))
 
 
 class DistributedModel:
@@ -402,9 +404,9 @@ def bench_multi(a):
             dm.energy_forces(pos)
         torch.cuda.synchronize()
         dist.barrier()
-        from . import _lib
+        from . import _lib, perf
         e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-        _lib.TIMED["facek_density_xm_fwd"] = []
+        perf.start()
         _lib.CALLS.clear()
         _lib.COUNTING = True
         with B.Clocks(local) as clk:
@@ -419,25 +421,18 @@ def bench_multi(a):
         _lib.COUNTING = False
         launches = torch.tensor([_lib.launches()], device=dev)
         dist.all_reduce(launches)                           # library kernels launched by all ranks
-        dens_ms = [s.elapsed_time(t) for s, t in _lib.TIMED.pop("facek_density_xm_fwd")]
         ms = torch.tensor([e0.elapsed_time(e1) / a.steps], device=dev)
         dist.all_reduce(ms, op=dist.ReduceOp.MAX)
         ms = float(ms)
-        # density-kernel roofline on this rank's local system (algorithmic bytes of one launch / launch time)
+        # roofline of the dominant kernels on this rank's local system (face_b200.perf)
         g = dm.graph
         El, Nl = int(g["ei"].numel()), int(g["row_ptr"].numel()) - 1
-        esz = 4 if dtype == torch.float32 else 8
-        Bb, Kk = spec["B"], spec["K"]
-        bytes_launch = esz * El * (Bb + Kk + 20) + esz * Nl * 20 * Bb * Kk + 4 * (Nl + 1)
-        pk = B.peaks()
-        hbm = pk.get("hbm_gbs", 6650.0)
-        achieved = bytes_launch / (statistics.mean(dens_ms) / 1e3) / 1e9 if dens_ms else None
-        traffic = None
-        tf = os.path.join(os.path.dirname(os.path.abspath(B.__file__)), "profiles", "density_fwd_traffic.json")
-        if os.path.exists(tf):
-            t = json.load(open(tf))
-            sc = t["small_case"]
-            traffic = (sc["dram_read_bytes"] * El / sc["edges"] + sc["dram_write_bytes"] * Nl / sc["atoms"])
+        root = os.path.dirname(os.path.abspath(B.__file__))
+        rows, pk = perf.collect(El, Nl, spec["B"], spec["K"], 4 if dtype == torch.float32 else 8, a.steps, root,
+                                traffic=perf.traffic_full_size(root, El, Nl))
+        roof = perf.headline(rows, pk)
+        if roof is not None:
+            roof["kernel"] += ", rank 0 local system"
         # e2e: positions from pinned host memory, decomposition + local neighbour list rebuilt, forces to the host
         e2e = None
         if not a.no_e2e:
@@ -470,11 +465,7 @@ def bench_multi(a):
                               "local_atoms_per_rank": [int(c) for c in allc],
                               "l2": "inputs larger than L2", "parallelism": f"spatial {dm.grid} over NCCL", "pme": dm.pme_mode},
                    "e2e": e2e, "energy": float(E), "clocks": clk.summary(),
-                   "roofline": {"kernel": "facek_density_xm_fwd (dens_fwd_k), rank 0 local system", "bound": "hbm",
-                                "achieved": achieved, "peak": hbm, "unit": "GB/s",
-                                "frac": achieved / hbm if achieved else None, "traffic": traffic,
-                                "bytes_per_launch": bytes_launch,
-                                "peak_source": "measured" if "hbm_gbs" in pk else "fallback"},
+                   "roofline": roof,
                    "gpu_launches": int(launches)}
             print(json.dumps(out), flush=True)
     finally:

@@ -7,8 +7,8 @@ same `set_*` / `fuse()` / `compile_radial()` switches, same graph-dict input and
 
 The edge-level work (geometry, radial basis x radial MLP, the factorised Cartesian density, directional
 messages, transport sums, their analytic backward and the force gather) runs in the hand-written CUDA
-kernels of libfacek.so behind a C ABI (face_b200._lib); node-level channel-mixing GEMMs run in cuBLAS;
-the node invariant algebra runs in its own kernel.  There is no CPU path: the model refuses to run on a
+kernels of libfacek.so behind a C ABI (face_b200._lib); in fp32 the node-level channel-mixing GEMMs run on the
+library's tcgen05 tensor-core GEMM (fp64 uses torch matmul); the node invariant algebra runs in its own kernel.  There is no CPU path: the model refuses to run on a
 device other than CUDA, and raises if the native library is missing.
 """
 import math

@@ -77,7 +77,35 @@ def _molecule_rows(pos64, sstart, astruct, rc, dtype):
     return rp, ei, ej, S, sh
 
 
-def build_graph(structures, rc, device="cuda", dtype=torch.float32):
+def structure_meta(sizes, cells, device):
+    """Host-side per-structure data the evaluation needs without reading the device: atom offsets, inverse cells and
+    volumes (host float64, and volumes also on the device) and lattice-vector lengths (for the PME mesh rule)."""
+    offs = [0]
+    for n in sizes:
+        offs.append(offs[-1] + int(n))
+    cells = np.asarray(cells, np.float64).reshape(-1, 3, 3)
+    inv, vol = [], []
+    for c in cells:
+        periodic = np.abs(c).sum() > 0
+        inv.append(np.linalg.inv(c) if periodic else np.zeros((3, 3)))
+        vol.append(abs(float(np.linalg.det(c))) if periodic else 0.0)
+    return {"offs": offs, "inv": inv, "vol": vol, "lengths": [np.linalg.norm(c, axis=1) for c in cells],
+            "vol_t": torch.as_tensor(vol, dtype=torch.float64, device=device)}
+
+
+def build_graph(structures, rc, device="cuda", dtype=torch.float32, skin=0.0):
+    """CSR neighbour graph of a batch of structures, built on the GPU (see module docstring).  With skin > 0 the
+    list holds every pair closer than rc + skin (for reuse across MD steps; "coul_cut" = rc keeps the Coulomb
+    real-space sum on the pairs closer than rc, and the model's envelope is zero beyond rc)."""
+    g = _build_graph(structures, rc + skin, device, dtype)
+    if skin > 0:
+        g["coul_cut"] = float(rc)
+        g["rc"] = float(rc)
+        g["skin"] = float(skin)
+    return g
+
+
+def _build_graph(structures, rc, device="cuda", dtype=torch.float32):
     """CSR neighbour graph of a batch of structures, built on the GPU (see module docstring)."""
     items = [_as_struct(s) for s in structures]
     if not items:
@@ -127,6 +155,7 @@ def build_graph(structures, rc, device="cuda", dtype=torch.float32):
         raise RuntimeError("neighbour list is not symmetric (reverse edge missing)")
     cells = np.stack([it[2] if it[3] else np.zeros((3, 3)) for it in items])
     return {"pos": torch.as_tensor(pos_np, dtype=dtype, device=dev), "pos64": pos64,
+            "meta": structure_meta(sizes, cells, dev),
             "Z": torch.as_tensor(np.concatenate([it[1] for it in items]), dtype=torch.long, device=dev),
             "batch": torch.as_tensor(np.repeat(np.arange(len(items)), sizes), dtype=torch.long, device=dev),
             "nstr": len(items), "natoms": torch.as_tensor(sizes, dtype=torch.long, device=dev),
@@ -192,8 +221,9 @@ def graph_from_padded(g):
         raise RuntimeError("graph_from_padded: neighbour list is not symmetric")
     natoms = torch.bincount(batch, minlength=nstr)
     cells = cell if cell is not None else torch.zeros(nstr, 3, 3, dtype=g["pos"].dtype, device=dev)
+    cell64 = cells.detach().double().cpu().numpy()
     return {"pos": g["pos"], "Z": g["Z"], "batch": batch, "nstr": nstr, "natoms": natoms, "cell": cells,
-            "cell64": cells.detach().double().cpu().numpy(),
+            "cell64": cell64, "meta": structure_meta(natoms.tolist(), cell64, dev),
             "pbc": [bool(c.abs().sum() > 0) for c in cells.detach().cpu()],
             "charge": g.get("charge", torch.zeros(nstr, dtype=g["pos"].dtype, device=dev)),
             "row_ptr": row_ptr, "ei": ei32, "ej": ej32, "S": S32, "shift": sh.contiguous(), "rev": rev}

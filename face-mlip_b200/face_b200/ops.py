@@ -314,17 +314,20 @@ class NodeAlgebraEngine(torch.autograd.Function):
 
 
 class CoulombReal(torch.autograd.Function):
-    """e_row[i] = 1/2 q_i sum_{e in row i} q_j (erf(r/gamma) - erf(r/gp))/r (face/electrostatics.py:91-92,125-127)."""
+    """e_row[i] = 1/2 q_i sum_{e in row i} q_j (erf(r/gamma) - erf(r/gp))/r (face/electrostatics.py:91-92,125-127).
+    A graph built with a skin (reused across MD steps) carries "coul_cut" = the model cutoff, so that the sum runs
+    over the same pairs as a fresh list; other graphs sum over every edge, as the reference does."""
 
     @staticmethod
     def forward(ctx, vec, q, gr, gamma, gp):
         N = q.shape[0]
         q = q.contiguous()
         e_row = torch.empty_like(q)
-        _lib.call("facek_coulomb_real_fwd", _tag(q), _p(vec), _p(gr["row_ptr"]), _p(gr["ej"]), _p(q), gamma, gp, N,
-                  _p(e_row), _lib.stream())
+        cut = float(gr.get("coul_cut") or 0.0)
+        _lib.call("facek_coulomb_real_fwd", _tag(q), _p(vec), _p(gr["row_ptr"]), _p(gr["ej"]), _p(q), gamma, gp, cut,
+                  N, _p(e_row), _lib.stream())
         ctx.save_for_backward(vec, q)
-        ctx.gr, ctx.gamma, ctx.gp = gr, gamma, gp
+        ctx.gr, ctx.gamma, ctx.gp, ctx.cut = gr, gamma, gp, cut
         return e_row
 
     @staticmethod
@@ -334,7 +337,7 @@ class CoulombReal(torch.autograd.Function):
         dvec = torch.empty_like(vec)
         dq = torch.empty_like(q)
         _lib.call("facek_coulomb_real_bwd", _tag(q), _p(vec), _p(ctx.gr["row_ptr"]), _p(ctx.gr["ej"]), _p(q),
-                  ctx.gamma, ctx.gp, _p(g_row), q.shape[0], _p(dvec), 0, _p(dq), _lib.stream())
+                  ctx.gamma, ctx.gp, ctx.cut, _p(g_row), q.shape[0], _p(dvec), 0, _p(dq), _lib.stream())
         return dvec, dq, None, None, None
 
 
@@ -358,11 +361,10 @@ class PMERecip(torch.autograd.Function):
     (torch.fft.rfftn) -> Green's function x |b|^2 (energy + convolved spectrum) -> irfftn -> gather."""
 
     @staticmethod
-    def forward(ctx, pos, q, cell64, gp, mesh):
+    def forward(ctx, pos, q, inv, vol, gp, mesh):
+        """inv: the cell's inverse (host float64 3x3), vol: its volume (host float), both fixed at graph build."""
         pos, q = pos.detach().contiguous(), q.detach().contiguous()
         n0, n1, n2 = mesh
-        inv = np.linalg.inv(cell64)
-        vol = abs(float(np.linalg.det(cell64)))
         invd = _lib.doubles(inv.reshape(-1))
         grid = torch.zeros(n0 * n1 * n2, dtype=pos.dtype, device=pos.device)
         _lib.call("facek_pme_spread", _tag(pos), _p(pos), _p(q), pos.shape[0], invd, n0, n1, n2, _p(grid),
@@ -387,7 +389,7 @@ class PMERecip(torch.autograd.Function):
         dpos = torch.empty_like(pos)
         _lib.call("facek_pme_gather", _tag(pos), _p(pos), _p(q), pos.shape[0], _lib.doubles(ctx.inv.reshape(-1)), n0,
                   n1, n2, _p(potg), 1.0, _p(dq), _p(dpos), _lib.stream())
-        return dpos, dq, None, None, None
+        return dpos, dq, None, None, None, None
 
 
 class SpreadMesh(torch.autograd.Function):
@@ -399,7 +401,7 @@ class SpreadMesh(torch.autograd.Function):
     def forward(ctx, pos, q, cell64, mesh):
         pos, q = pos.detach().contiguous(), q.detach().contiguous()
         n0, n1, n2 = mesh
-        inv = np.linalg.inv(cell64)
+        inv = np.linalg.inv(cell64)         # host-side 3x3 (the slab PME passes a constant cell)
         grid = torch.zeros(n0 * n1 * n2, dtype=pos.dtype, device=pos.device)
         _lib.call("facek_pme_spread", _tag(pos), _p(pos), _p(q), pos.shape[0], _lib.doubles(inv.reshape(-1)), n0,
                   n1, n2, _p(grid), _lib.stream())
@@ -670,6 +672,17 @@ def per_atom(v, batch, nstr):
     return v[batch]
 
 
+def cell_meta(gr):
+    """Host-side per-structure data of a graph: atom offsets, inverse cells, volumes (host and device), lattice
+    lengths.  Graphs from build_graph carry it from construction; other graphs get it here once (one host read)."""
+    meta = gr.get("meta")
+    if meta is None:
+        from .neighbors import structure_meta
+        meta = structure_meta([int(n) for n in gr["natoms"].tolist()], gr["cell64"], gr["pos"].device)
+        gr["meta"] = meta
+    return meta
+
+
 def coulomb_term(P, gr, geo, h, pos):
     """LatentCharges.forward, mode 'local' (face/electrostatics.py:132-176)."""
     c = P["coulomb"]
@@ -696,18 +709,21 @@ def coulomb_term(P, gr, geo, h, pos):
     e_real = seg_sum(e_row, batch, nstr)
     q2 = seg_sum(q * q, batch, nstr)
     qs = seg_sum(q, batch, nstr)
+    # per-structure host data (atom offsets, inverse cells, volumes, PME meshes) was fixed when the graph was built,
+    # so this loop launches kernels without reading anything back from the device (the reference's per-structure
+    # loop, face/electrostatics.py:144-146, syncs on nonzero()/item())
+    meta = cell_meta(gr)
+    offs = meta["offs"]
     e_recip = []
-    offs = [0] + np.cumsum(natoms.tolist()).tolist()
     for s in range(nstr):
-        cell = gr["cell64"][s]
         mesh = c["mesh"]
         if mesh is None:                                       # face/electrostatics.py:56-58
             spacing = gp / 4.0
-            mesh = tuple(max(8, int(math.ceil(float(L) / spacing))) for L in np.linalg.norm(cell, axis=1))
+            mesh = tuple(max(8, int(math.ceil(float(L) / spacing))) for L in meta["lengths"][s])
         sl = slice(offs[s], offs[s + 1])
-        e_recip.append(PMERecip.apply(pos[sl], q[sl], cell, gp, tuple(mesh)))
+        e_recip.append(PMERecip.apply(pos[sl], q[sl], meta["inv"][s], meta["vol"][s], gp, tuple(mesh)))
     e_recip = torch.stack(e_recip)
-    vol = torch.as_tensor([abs(np.linalg.det(gr["cell64"][s])) for s in range(nstr)], dtype=q.dtype, device=q.device)
+    vol = meta["vol_t"].to(q.dtype)
     e_es = KE * (e_recip + e_real - q2 / (math.sqrt(math.pi) * gp) - 0.5 * math.pi * gp ** 2 / vol * qs ** 2)
     return chi * q + 0.5 * J * q * q + per_atom(e_es / natoms.to(q.dtype), batch, nstr), q
 

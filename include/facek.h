@@ -132,10 +132,12 @@ int facek_nlist_reverse(const int32_t* row_ptr, const int32_t* ei, const int32_t
  * themselves (a host framework that hands out only preallocated buffers, or code running inside a memory pool
  * or arena that forbids cudaMalloc).  The scratch lives in a file-scope device array of about 7.1 MB that every
  * GPU loading the library holds until exit; limits: N <= 262,144 atoms and <= 65,536 cells.  The caller passes
- * row_ptr (N+1) and output buffers of capacity max_edges; *n_edges receives the edge count (also when it exceeds
- * max_edges, which returns FACEK_EINVAL with nothing filled, so the caller can retry with larger buffers).
- * Calls no cudaMalloc/cudaFree.  The first call on a device looks up the scratch address (cudaGetSymbolAddress)
- * and should come before any stream capture; the call synchronises the stream twice (edge count, error flag).
+ * row_ptr (N+1) and output buffers of capacity max_edges; *n_edges receives the edge count.  When that count exceeds
+ * max_edges the call returns FACEK_EINVAL with ei/ej/S/shift untouched but row_ptr already written (the caller can
+ * retry with larger buffers); a row longer than 512 neighbours returns FACEK_EUNSUPPORTED before any edge is
+ * written (*n_edges = -1).  Calls no cudaMalloc/cudaFree.  The scratch's device address is looked up
+ * (cudaGetSymbolAddress) on every call with the caller's device current.  The call synchronises the stream twice
+ * (edge count, error flags), so it cannot be captured into a CUDA graph.
  * All calls share the scratch array: calls that overlap on the GPU (other streams, other host threads) race. */
 int facek_nlist_cell_build_noalloc(int dtype, const double* pos, int64_t N, const double* cell, double rc,
                                    int64_t max_edges, int32_t* row_ptr, int32_t* ei, int32_t* ej, int32_t* S,
@@ -233,6 +235,8 @@ int facek_transport_bwd(int dtype, const void* phi, const void* vec, const int32
  * conv = G*B*F * (n0 n1 n2 / V) so that irfftn(conv) is the mesh potential dE/dQ.  bmod: |b(m)|^-2 per axis
  * concatenated (n0 + n1 + n2).  gather: dq[i] = scale sum W phi, dpos[i] = scale q_i sum grad W phi.
  * Real space: e_row[i] = 1/2 q_i sum_{e in row i} q_j K(r_e); the adjoint takes the per-row upstream g_row.
+ * r_cut > 0 drops edges with r >= r_cut (a neighbour list built with a skin and reused across MD steps gives the
+ * same sum as a fresh list at the model cutoff); r_cut <= 0 keeps every edge, as the reference does with its pairs.
  */
 int facek_pme_spread(int dtype, const void* pos, const void* q, int64_t N, const double* inv, int32_t n0,
                      int32_t n1, int32_t n2, void* mesh, void* stream);
@@ -242,10 +246,10 @@ int facek_pme_gather(int dtype, const void* pos, const void* q, int64_t N, const
                      int32_t n1, int32_t n2, const void* potential, double scale, void* dq, void* dpos,
                      void* stream);
 int facek_coulomb_real_fwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej, const void* q,
-                           double gamma, double gp, int64_t N, void* e_row, void* stream);
+                           double gamma, double gp, double r_cut, int64_t N, void* e_row, void* stream);
 int facek_coulomb_real_bwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej, const void* q,
-                           double gamma, double gp, const void* g_row, int64_t N, void* dvec, int32_t accumulate,
-                           void* dq, void* stream);
+                           double gamma, double gp, double r_cut, const void* g_row, int64_t N, void* dvec,
+                           int32_t accumulate, void* dq, void* stream);
 
 #ifdef __cplusplus
 }

@@ -1,7 +1,7 @@
 """Generate golden fixtures from the face-mlip reference itself (run in a container that has the reference
 checked out; the fixtures are committed, the reference is not needed to run the tests).
 
-    python tests/golden/make_golden.py [--ref /path/to/face-mlip]
+    python tests/golden/make_golden.py --ref /path/to/face-mlip [--only NAME]
 
 For every case: seeded structure (face_b200.systems) -> canonical neighbour list (oracle.nlist, the
 reference's ASE call is not installed) -> the reference's own FACE (face/model.py) with seeded weights
@@ -35,7 +35,13 @@ CASES = [
     ("cfg3_small", 3, 6, {}, None, False),
     ("cfg4_small", 4, 600, {}, (24, 24, 24), False),
     ("cfg5_small", 5, 4, {}, (24, 24, 24), False),
+    # the benchmark configurations at their full size (cfg3, cfg4 at L = 3) and a 37,044-atom cfg5 sub-box
+    # (21^3 conventional cells, PME mesh at the 256^3 spacing of the full alloy: 75.6 A / 84 = 230.4 A / 256)
+    ("cfg3", 3, None, {}, None, False),
+    ("cfg4", 4, None, {}, (96, 96, 96), False),
+    ("cfg5_37k", 5, 21, {}, (84, 84, 84), False),
 ]
+BIG = 4000          # cases above this many atoms store a position hash instead of the positions
 
 
 def build_reference_model(face_model, cfg, over, state):
@@ -104,9 +110,17 @@ def run_model_case(ref, name, cfg, scale, over, mesh, spline, seed=0):
     meta = {"cfg": cfg, "scale": scale, "seed": seed, "over": over, "mesh": mesh, "spline": spline,
             "spec": spec, "pme": {k: (list(v) if isinstance(v, tuple) else v) for k, v in pme.items()},
             "n_edges": int(len(edges)), "M": int(g["nbr"].shape[1])}
+    pos = np.concatenate([s.positions for s in structs])
+    if len(pos) > BIG:
+        # large cases: the positions are regenerated from the seed and checked against this hash; fp32 outputs are
+        # kept in float32 (their own precision)
+        geo = {"pos_sha256": np.array(_hash(np.ascontiguousarray(pos, np.float64)))}
+        out = {k: (v.astype(np.float32) if k.endswith("32") else v) for k, v in out.items()}
+    else:
+        geo = {"pos": pos}
     np.savez_compressed(os.path.join(HERE, name + ".npz"), meta=json.dumps(meta),
-                        pos=np.concatenate([s.positions for s in structs]),
-                        Z=np.concatenate([s.numbers for s in structs]), edge_hash=np.array(_hash(edges)), **out)
+                        Z=np.concatenate([s.numbers for s in structs]), edge_hash=np.array(_hash(edges)), **geo,
+                        **out)
     print(f"{name}: N={len(g['pos'])} E={len(edges)} M={g['nbr'].shape[1]}  E64={out['energy64'][:3]}  "
           f"|F|max={np.abs(out['forces64']).max():.3e}  dE32/E={np.abs(out['energy32'] - out['energy64']).max() / np.abs(out['energy64']).max():.1e}")
 
@@ -187,7 +201,7 @@ def electrostatics_cases(ref):
 
 def main():
     ap = argparse.ArgumentParser()
-    ap.add_argument("--ref", default="/root/reference")
+    ap.add_argument("--ref", required=True, help="checkout of the face-mlip reference (read-only)")
     ap.add_argument("--only", default="")
     a = ap.parse_args()
     if not os.path.isdir(os.path.join(a.ref, "face")):
@@ -195,7 +209,7 @@ def main():
     sys.path.insert(0, a.ref)
     torch.set_num_threads(max(1, os.cpu_count()))
     for c in CASES:
-        if not a.only or a.only in c[0]:
+        if not a.only or a.only == c[0] or (a.only.endswith("*") and c[0].startswith(a.only[:-1])):
             run_model_case(a.ref, *c)
     if not a.only or a.only == "kernels":
         kernel_cases(a.ref)

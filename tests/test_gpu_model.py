@@ -40,6 +40,19 @@ def _run(name, dtype):
 
 
 @pytest.mark.parametrize("name", MODEL_CASES)
+def test_neighbour_list_matches_golden_edges(name):
+    """The GPU cell list gives, bit for bit, the (i, j, S) edge list (canonical row order) that the reference's model
+    consumed when the golden was made: the fixture holds the SHA-256 of that int64 (E, 5) array."""
+    import hashlib
+    from face_b200.neighbors import build_graph
+    structs, spec, pme, d = case_inputs(name)
+    g = build_graph(structs, spec["rc"], dtype=torch.float64)
+    edges = torch.cat([g["ei"][:, None], g["ej"][:, None], g["S"]], 1).to(torch.int64).cpu().numpy()
+    assert len(edges) == d["meta"]["n_edges"]
+    assert hashlib.sha256(np.ascontiguousarray(edges).tobytes()).hexdigest() == str(d["edge_hash"])
+
+
+@pytest.mark.parametrize("name", MODEL_CASES)
 def test_fp64_matches_reference(name):
     o, d = _run(name, torch.float64)
     E, F = o["energy"].cpu().numpy(), o["forces"].cpu().numpy()
@@ -48,15 +61,22 @@ def test_fp64_matches_reference(name):
     assert np.abs(o["atom_energy"].cpu().numpy() - d["atom_energy64"]).max() <= 1e-9
 
 
-@pytest.mark.parametrize("name", [c for c in MODEL_CASES if c != "cfg1_spline"])
+@pytest.mark.parametrize("name", MODEL_CASES)
 def test_fp32_matches_reference(name):
+    """fp32 bars: energy within 1e-6 relative, forces within 1e-4 eV/A.  Model cases are held to both the reference's
+    fp64 and fp32 outputs.  The compiled-radial case is held to the reference's fp32 outputs: its Hermite tables are
+    built in the model's precision (face/model.py:393-405), so the fp32 spline is a different function from the fp64
+    one at the 1e-7 level of the table entries."""
     o, d = _run(name, torch.float32)
     E, F = o["energy"].double().cpu().numpy(), o["forces"].double().cpu().numpy()
     scale = np.abs(d["energy64"]).max()
-    assert np.abs(E - d["energy64"]).max() <= 1e-6 * scale, (E, d["energy64"])
-    assert np.abs(E - d["energy32"]).max() <= 1e-6 * scale
-    dF = np.abs(F - d["forces64"]).max()
-    assert dF <= 1e-4 and dF <= 1e-4 * max(1.0, np.abs(d["forces64"]).max()), dF
+    refs = [("32", d["energy32"], d["forces32"])]
+    if not d["meta"]["spline"]:
+        refs.append(("64", d["energy64"], d["forces64"]))
+    for tag, Er, Fr in refs:
+        assert np.abs(E - Er).max() <= 1e-6 * scale, (tag, E, Er)
+        dF = np.abs(F - Fr).max()
+        assert dF <= 1e-4 and dF <= 1e-4 * max(1.0, np.abs(Fr).max()), (tag, dF)
 
 
 def test_reference_padded_graph_input():

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from _golden import MODEL_CASES, case_inputs, load
+from _golden import SMALL_CASES, case_inputs, load
 from oracle import face_ref, nlist
 
 
@@ -18,7 +18,7 @@ def _engine_state(spec, seed):
     return m.seed_(seed).state_dict()
 
 
-@pytest.mark.parametrize("name", MODEL_CASES)
+@pytest.mark.parametrize("name", SMALL_CASES)
 def test_oracle_matches_reference(name):
     structs, spec, pme, d = case_inputs(name)
     g = nlist.padded_graph(structs, spec["rc"])

@@ -76,3 +76,31 @@ def test_noalloc_rejects_out_of_range_sizes():
     # still usable afterwards
     rp1, ei1, *_ = _noalloc(st, 5.0, torch.float32, capacity=ei0.numel())
     assert _same(rp1, rp0) and _same(ei1, ei0)
+
+
+def test_noalloc_rejects_too_many_cells_and_long_rows():
+    """The cell-count limit is checked on the host before any GPU work; a row with more than 512 neighbours is caught
+    in the counting pass, before row offsets are used and before any edge is written."""
+    from face_b200 import _lib, systems
+    rng = np.random.default_rng(11)
+    sparse = systems.Structure(rng.uniform(0, 100.0, (100, 3)), np.ones(100, np.int64), np.eye(3) * 100.0, True)
+    with pytest.raises(RuntimeError, match="cells exceed the limit"):
+        _noalloc(sparse, 1.0, torch.float32, capacity=1000)          # 99^3 cells of width >= rc
+    dense = systems.Structure(rng.uniform(0, 10.0, (800, 3)), np.ones(800, np.int64), np.eye(3) * 10.0, True)
+    pos64 = torch.as_tensor(dense.positions, dtype=torch.float64, device="cuda").contiguous()
+    cap = 1 << 20
+    row_ptr = torch.zeros(801, dtype=torch.int32, device="cuda")
+    ei = torch.full((cap,), -7, dtype=torch.int32, device="cuda")
+    ej, S = torch.full_like(ei, -7), torch.full((cap, 3), -7, dtype=torch.int32, device="cuda")
+    sh = torch.zeros(cap, 3, dtype=torch.float32, device="cuda")
+    n_edges = ctypes.c_int64(0)
+    with pytest.raises(RuntimeError, match="more than 512 neighbours"):   # ~720 neighbours per atom at rc = 6
+        _lib.call("facek_nlist_cell_build_noalloc", 0, _lib.ptr(pos64), 800,
+                  _lib.doubles(np.asarray(dense.cell, np.float64).reshape(-1)), 6.0, cap, _lib.ptr(row_ptr),
+                  _lib.ptr(ei), _lib.ptr(ej), _lib.ptr(S), _lib.ptr(sh), ctypes.byref(n_edges), _lib.stream())
+    assert n_edges.value == -1
+    assert bool((ei == -7).all()) and bool((ej == -7).all())              # nothing filled
+    st = systems.config_structures(5, seed=1, scale=4)[0]                  # the shared scratch is reusable after
+    rp0, ei0, *_ = _regular(st, 5.0, torch.float32)
+    rp1, ei1, *_ = _noalloc(st, 5.0, torch.float32, capacity=ei0.numel())
+    assert _same(rp1, rp0) and _same(ei1, ei0)
