@@ -214,6 +214,110 @@ __global__ void __launch_bounds__(128) radial_mlp_k(const T* __restrict__ vec, c
   }
 }
 
+// Wide output layer (B > 32: the CP form's B + 4C radial functions, face/model.py:449, and the non-factorised
+// block's 4C or 8C, face/model.py:130): both hidden layers and their r-tangents stay in registers, and the output
+// rows of W3 are read as warp-uniform broadcasts from global memory (L1-resident) one output at a time.
+template <typename T, int NBMAX, int HMAX>
+__global__ void __launch_bounds__(128) radial_wide_k(const T* __restrict__ vec, const int32_t* __restrict__ ei,
+                                                     const int32_t* __restrict__ ej, const int32_t* __restrict__ zidx,
+                                                     int n_el, T rc, int nb, int H, int B, const T* __restrict__ w1,
+                                                     const T* __restrict__ b1, const T* __restrict__ pair,
+                                                     const T* __restrict__ w2, const T* __restrict__ b2,
+                                                     const T* __restrict__ w3, const T* __restrict__ b3,
+                                                     T* __restrict__ phi, T* __restrict__ dphidr, int64_t E) {
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  T* sW1 = reinterpret_cast<T*>(smem_raw);   // H x nb
+  T* sB1 = sW1 + H * nb;                      // H
+  T* sPair = sB1 + H;                         // n_el^2 x H
+  T* sW2 = sPair + n_el * n_el * H;           // H x H
+  T* sB2 = sW2 + H * H;                       // H
+  for (int q = threadIdx.x; q < H * nb; q += blockDim.x) sW1[q] = w1[q];
+  for (int q = threadIdx.x; q < H; q += blockDim.x) { sB1[q] = b1[q]; sB2[q] = b2[q]; }
+  for (int q = threadIdx.x; q < n_el * n_el * H; q += blockDim.x) sPair[q] = pair[q];
+  for (int q = threadIdx.x; q < H * H; q += blockDim.x) sW2[q] = w2[q];
+  __syncthreads();
+  const T c = sqrt(T(2) / rc);
+  const T pi = T(3.14159265358979323846);
+  // every thread runs the same number of loop trips so the output loop's W3 reads stay warp-uniform
+  const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+  for (int64_t e0 = (int64_t)blockIdx.x * blockDim.x; e0 < E; e0 += stride) {
+    const int64_t e = e0 + threadIdx.x;
+    const bool live = e < E;
+    const int64_t ee = live ? e : E - 1;
+    const T vx = vec[ee * 3], vy = vec[ee * 3 + 1], vz = vec[ee * 3 + 2];
+    const T r = sqrt(vx * vx + vy * vy + vz * vz);
+    T env, denv;
+    envelope(r, rc, env, denv);
+    T rb[NBMAX], drb[NBMAX];
+#pragma unroll
+    for (int n = 0; n < NBMAX; n++) {
+      rb[n] = 0;
+      drb[n] = 0;
+      if (n < nb) {
+        const T f = T(n + 1) * pi / rc;
+        const T s = sin(f * r), co = cos(f * r);
+        const T bes = s / r * c;
+        const T dbes = (f * co / r - s / (r * r)) * c;
+        rb[n] = bes * env;
+        drb[n] = dbes * env + bes * denv;
+      }
+    }
+    const T* prow = sPair + (zidx[ei[ee]] * n_el + zidx[ej[ee]]) * H;
+    T a1[HMAX], da1[HMAX];
+#pragma unroll
+    for (int h = 0; h < HMAX; h++) {
+      a1[h] = 0;
+      da1[h] = 0;
+      if (h < H) {
+        T z = sB1[h] + prow[h], dz = 0;
+#pragma unroll
+        for (int n = 0; n < NBMAX; n++)
+          if (n < nb) {
+            z += sW1[h * nb + n] * rb[n];
+            dz += sW1[h * nb + n] * drb[n];
+          }
+        const T sg = sigmoid(z);
+        a1[h] = z * sg;
+        da1[h] = sg * (T(1) + z * (T(1) - sg)) * dz;
+      }
+    }
+    T a2[HMAX], da2[HMAX];
+#pragma unroll
+    for (int o = 0; o < HMAX; o++) {
+      a2[o] = 0;
+      da2[o] = 0;
+      if (o < H) {
+        T z = sB2[o], dz = 0;
+#pragma unroll
+        for (int h = 0; h < HMAX; h++)
+          if (h < H) {
+            z += sW2[o * H + h] * a1[h];
+            dz += sW2[o * H + h] * da1[h];
+          }
+        const T sg = sigmoid(z);
+        a2[o] = z * sg;
+        da2[o] = sg * (T(1) + z * (T(1) - sg)) * dz;
+      }
+    }
+#pragma unroll 1
+    for (int b = 0; b < B; b++) {
+      const T* wrow = w3 + (int64_t)b * H;
+      T z = __ldg(b3 + b), dz = 0;
+#pragma unroll
+      for (int h = 0; h < HMAX; h++)
+        if (h < H) {
+          const T w = __ldg(wrow + h);
+          z += w * a2[h];
+          dz += w * da2[h];
+        }
+      if (live) {
+        phi[e * B + b] = z * env;
+        dphidr[e * B + b] = dz * env + z * denv;
+      }
+    }
+  }
+}
+
 template <typename T, int BMAX>
 __global__ void radial_spline_k(const T* __restrict__ vec, const int32_t* __restrict__ ei,
                                 const int32_t* __restrict__ ej, const int32_t* __restrict__ zidx, int n_el, T rc,
@@ -876,12 +980,34 @@ int radial_launch(const void* vec, const int32_t* ei, const int32_t* ej, const i
   return launch_status("facek_radial_fwd");
 }
 
+template <typename T, int NBMAX>
+int radial_wide_launch(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el,
+                       double rc, int nb, int H, int B, const void* w1, const void* b1, const void* pair,
+                       const void* w2, const void* b2, const void* w3, const void* b3, void* phi, void* dphidr,
+                       int64_t E, void* stream) {
+  const size_t smem = sizeof(T) * ((size_t)H * nb + 2 * H + (size_t)n_el * n_el * H + (size_t)H * H);
+  FACEK_CHECK_ARG((int)smem <= max_smem_optin(), "facek_radial_fwd: weights (%zu B) exceed shared memory", smem);
+  if (smem > 48 * 1024)
+    cudaFuncSetAttribute(radial_wide_k<T, NBMAX, 64>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
+  radial_wide_k<T, NBMAX, 64><<<grid_for(ceil_div<int64_t>(E, 128), 4), 128, smem, as_stream(stream)>>>(
+      (const T*)vec, ei, ej, zidx, n_el, (T)rc, nb, H, B, (const T*)w1, (const T*)b1, (const T*)pair, (const T*)w2,
+      (const T*)b2, (const T*)w3, (const T*)b3, (T*)phi, (T*)dphidr, E);
+  return launch_status("facek_radial_fwd");
+}
+
 template <typename T>
 int radial_simt(const void* vec, const int32_t* ei, const int32_t* ej, const int32_t* zidx, int n_el, double rc,
                 int nb, int H, int B, const void* w1, const void* b1, const void* pair, const void* w2, const void* b2,
                 const void* w3, const void* b3, void* phi, void* dphidr, int64_t E, void* stream) {
   if (E == 0) return FACEK_OK;
-  FACEK_CHECK_ARG(H <= 64 && B <= 32 && nb <= 16, "facek_radial_fwd: H=%d B=%d nb=%d exceed 64/32/16", H, B, nb);
+  FACEK_CHECK_ARG(H <= 64 && nb <= 16, "facek_radial_fwd: H=%d nb=%d exceed 64/16", H, nb);
+  if (B > 32) {
+    if (nb <= 8)
+      return radial_wide_launch<T, 8>(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
+                                      dphidr, E, stream);
+    return radial_wide_launch<T, 16>(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
+                                     dphidr, E, stream);
+  }
   if (nb <= 8 && B <= 16)
     return radial_launch<T, 8, 64, 16>(vec, ei, ej, zidx, n_el, rc, nb, H, B, w1, b1, pair, w2, b2, w3, b3, phi,
                                        dphidr, E, stream);

@@ -60,6 +60,12 @@ SIGNATURES = {
     "facek_pme_spread": [I32, P, P, I64, PD, I32, I32, I32, P, P],
     "facek_pme_green": [I32, P, I32, I32, I32, PD, D, D, P, P, P, P],
     "facek_pme_gather": [I32, P, P, I64, PD, I32, I32, I32, P, D, P, P, P],
+    "facek_cp_density_fwd": [I32, P, P, I64, I32, P, P, I64, I32, P, P],
+    "facek_cp_density_bwd": [I32, P, P, I64, I32, P, P, P, P, I64, I64, I32, P, P, P, P],
+    "facek_zbl_fwd": [I32, P, P, P, P, D, D, I64, P, P],
+    "facek_zbl_bwd": [I32, P, P, P, P, D, D, P, I64, P, I32, P],
+    "facek_disp_fwd": [I32, P, P, P, P, P, P, D, I64, P, P],
+    "facek_disp_bwd": [I32, P, P, P, P, P, P, D, P, I64, P, I32, P, P],
     "facek_coulomb_real_fwd": [I32, P, P, P, P, D, D, D, I64, P, P],
     "facek_coulomb_real_bwd": [I32, P, P, P, P, D, D, D, P, I64, P, I32, P, P],
 }

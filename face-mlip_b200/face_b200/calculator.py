@@ -104,7 +104,9 @@ class FACECalculator(Calculator):
             g = self._graph
             if 2.0 * float((p64 - g["pos64"]).norm(dim=1).max()) < self.skin:
                 return dict(g, pos=p64.to(self.dtype))
-        self._graph = build_graph([at], self.model.rc, device=self.device, dtype=self.dtype, skin=self.skin)
+        rc_long = self.model.terms["disp"].r_long if "disp" in self.model.terms else None
+        self._graph = build_graph([at], self.model.rc, device=self.device, dtype=self.dtype, skin=self.skin,
+                                  rc_long=rc_long)
         self._key = key
         self.rebuilds += 1
         return self._graph

@@ -18,7 +18,7 @@ import torch.nn as nn
 import torch.nn.functional as F
 
 from . import ops
-from .params import BlockParams, Bessel, ChargeParams, seeded_state
+from .params import BlockParams, Bessel, ChargeParams, DispParams, ZBLParams, seeded_state
 
 BODY_ORDER = [2, 3, 3, 3, 4, 4, 4, 4, 5]          # face/model.py:246,268
 RANK_SLICE = {0: slice(0, 1), 1: slice(1, 4), 2: slice(4, 10), 3: slice(10, 20)}
@@ -30,10 +30,7 @@ class FACE(nn.Module):
     def __init__(self, elements, C=64, n_basis=8, rc=5.0, n_passes=2, terms=(), radial_hidden=64, K_dir=16,
                  norm="layer", transport=False, eqmsg=False, factor=False, B=16, K=32, cp=False, unit=False):
         super().__init__()
-        if not factor:
-            raise NotImplementedError("the B200 engine implements the factorised block (factor=True)")
-        if cp:
-            raise NotImplementedError("CP density form (cp=True) is not implemented in the B200 engine")
+        self.form = ("cp" if cp else "factor") if factor else "moment"      # face/model.py:568-569
         self.rc, self.C, self.n_passes, self.elements = rc, C, n_passes, list(elements)
         self.B, self.K, self.K_dir, self.n_basis = B, K, K_dir, n_basis
         self.transport, self.eqmsg, self.norm_kind = transport, eqmsg, norm
@@ -49,17 +46,24 @@ class FACE(nn.Module):
         self.embed = nn.Embedding(n_el, C)
         self.blocks = nn.ModuleList([
             BlockParams(C, n_basis, t + 1, radial_hidden, n_el, K_dir, norm, transport,
-                        eq_in=eqmsg and t > 0, eq_out=eqmsg and t < n_passes - 1, B=B, K=K)
+                        eq_in=eqmsg and t > 0, eq_out=eqmsg and t < n_passes - 1, B=B, K=K, form=self.form)
             for t in range(n_passes)])
         self.register_buffer("E0", torch.zeros(n_el))
         self.register_buffer("scale", torch.tensor(1.0))
         self.register_buffer("avg_nb", torch.tensor(10.0))
         self.terms = nn.ModuleDict()
-        for t in terms:
+        for t in terms:                                  # face/model.py:580-590, evaluated in this order
             if t == "coulomb":
                 self.terms[t] = ChargeParams(C)
+            elif t == "zbl":
+                self.terms[t] = ZBLParams()
+            elif t == "disp":
+                self.terms[t] = DispParams(C)
+            elif t == "qeq":
+                raise NotImplementedError("the 'qeq' term (LatentCharges mode 'full', an O(N^3) charge solve) is not "
+                                          "implemented in the B200 engine")
             else:
-                raise NotImplementedError(f"physics term {t!r} is not implemented in the B200 engine")
+                raise ValueError(t)
         self.spline = [None] * n_passes
         self._prepared = None
 
@@ -105,7 +109,7 @@ class FACE(nn.Module):
     def compile_radial(self, n_grid=4096, on=True):
         """Tabulate each block's radial MLP per element pair (cubic Hermite, face/model.py:644-655)."""
         self.spline = [None] * self.n_passes
-        if on:
+        if on and self.form != "moment":               # the non-factorised block has no compiled radial
             for t in range(self.n_passes):
                 self.spline[t] = ops.build_spline(self, t, n_grid)
         self._prepared = None

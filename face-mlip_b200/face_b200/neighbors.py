@@ -93,15 +93,22 @@ def structure_meta(sizes, cells, device):
             "vol_t": torch.as_tensor(vol, dtype=torch.float64, device=device)}
 
 
-def build_graph(structures, rc, device="cuda", dtype=torch.float32, skin=0.0):
+LR_KEYS = ("row_ptr", "ei", "ej", "S", "shift", "rev")
+
+
+def build_graph(structures, rc, device="cuda", dtype=torch.float32, skin=0.0, rc_long=None):
     """CSR neighbour graph of a batch of structures, built on the GPU (see module docstring).  With skin > 0 the
     list holds every pair closer than rc + skin (for reuse across MD steps; "coul_cut" = rc keeps the Coulomb
-    real-space sum on the pairs closer than rc, and the model's envelope is zero beyond rc)."""
+    real-space sum on the pairs closer than rc, and the model's envelope is zero beyond rc).  rc_long adds the
+    long-range pair list of the dispersion term under "lr" (face/datasets.py:53-55, GraphSet(rc_long=...))."""
     g = _build_graph(structures, rc + skin, device, dtype)
     if skin > 0:
         g["coul_cut"] = float(rc)
         g["rc"] = float(rc)
         g["skin"] = float(skin)
+    if rc_long:
+        lr = _build_graph(structures, rc_long + skin, device, dtype)
+        g["lr"] = {k: lr[k] for k in LR_KEYS}
     return g
 
 
@@ -189,17 +196,9 @@ def padded_graph(atoms_list, rc, device="cuda", dtype=torch.float32, skin=0.0):
     return to_padded(build_graph(atoms_list, rc + skin, device, dtype))
 
 
-def graph_from_padded(g):
-    """Reference padded graph dict -> engine CSR graph (edges re-ordered canonically within rows)."""
-    nbr, mask, shift = g["nbr"], g["mask"], g["shift"]
-    dev = nbr.device
-    N, M = nbr.shape
-    ei = torch.arange(N, device=dev)[:, None].expand(N, M)[mask]
-    ej = nbr[mask]
-    sh = shift[mask]
-    batch = g["batch"]
-    nstr = int(g["nstr"]) if "nstr" in g else int(batch.max()) + 1
-    cell = g.get("cell")
+def _csr_from_pairs(ei, ej, sh, batch, cell, N):
+    """(i, j, shift) pairs -> canonical CSR rows (i, j, S0, S1, S2 order) with the reverse-edge index."""
+    dev = ei.device
     S = torch.zeros(ei.numel(), 3, dtype=torch.int64, device=dev)
     if cell is not None and bool((cell.abs().sum((1, 2)) > 0).any()):
         c64 = cell.detach().double().cpu().numpy()
@@ -219,11 +218,28 @@ def graph_from_padded(g):
               _lib.ptr(rev), _lib.stream())
     if E and bool((rev < 0).any()):
         raise RuntimeError("graph_from_padded: neighbour list is not symmetric")
+    return {"row_ptr": row_ptr, "ei": ei32, "ej": ej32, "S": S32, "shift": sh.contiguous(), "rev": rev}
+
+
+def graph_from_padded(g):
+    """Reference padded graph dict -> engine CSR graph (edges re-ordered canonically within rows); the long-range
+    pair list lr_i / lr_j / lr_shift (face/datasets.py:92-95), when present, becomes g["lr"]."""
+    nbr, mask, shift = g["nbr"], g["mask"], g["shift"]
+    dev = nbr.device
+    N, M = nbr.shape
+    ei = torch.arange(N, device=dev)[:, None].expand(N, M)[mask]
+    ej = nbr[mask]
+    sh = shift[mask]
+    batch = g["batch"]
+    nstr = int(g["nstr"]) if "nstr" in g else int(batch.max()) + 1
+    cell = g.get("cell")
+    csr = _csr_from_pairs(ei, ej, sh, batch, cell, N)
     natoms = torch.bincount(batch, minlength=nstr)
     cells = cell if cell is not None else torch.zeros(nstr, 3, 3, dtype=g["pos"].dtype, device=dev)
     cell64 = cells.detach().double().cpu().numpy()
     return {"pos": g["pos"], "Z": g["Z"], "batch": batch, "nstr": nstr, "natoms": natoms, "cell": cells,
             "cell64": cell64, "meta": structure_meta(natoms.tolist(), cell64, dev),
             "pbc": [bool(c.abs().sum() > 0) for c in cells.detach().cpu()],
-            "charge": g.get("charge", torch.zeros(nstr, dtype=g["pos"].dtype, device=dev)),
-            "row_ptr": row_ptr, "ei": ei32, "ej": ej32, "S": S32, "shift": sh.contiguous(), "rev": rev}
+            "charge": g.get("charge", torch.zeros(nstr, dtype=g["pos"].dtype, device=dev)), **csr,
+            **({"lr": _csr_from_pairs(g["lr_i"].long(), g["lr_j"].long(), g["lr_shift"].to(g["pos"].dtype), batch,
+                                      cell, N)} if "lr_i" in g else {})}

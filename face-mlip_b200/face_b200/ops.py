@@ -88,7 +88,7 @@ class Radial(torch.autograd.Function):
     @staticmethod
     def forward(ctx, vec, gr, blk):
         E = vec.shape[0]
-        B = blk["B"]
+        B = blk["R"]                               # radial outputs: B, or B + 4C (CP), or 4C / 8C (non-factorised)
         phi = torch.empty(E, B, dtype=vec.dtype, device=vec.device)
         dphidr = torch.empty_like(phi)
         if blk.get("spline") is not None:
@@ -215,6 +215,63 @@ class DensityMsg(torch.autograd.Function):
         return dphi, dY, dTJ, dTI, None
 
 
+class CPDensity(torch.autograd.Function):
+    """Per-channel density D[x, i, c] = sum_{e in row i} Y[e,x] R[e, l(x), c] m[e, c] of the CP form and the
+    non-factorised block (face/model.py:496-502, :182-187): R = columns r_off .. r_off + 4C of the radial output phi
+    (envelope included), m (E, C) the edge message.  Returns the four rank blocks (k_l, N, C) of one (20, N, C)
+    buffer; the adjoint returns a full-width dphi whose other columns are zero."""
+
+    @staticmethod
+    def forward(ctx, Y, phi, r_off, m, gr):
+        N = gr["row_ptr"].numel() - 1
+        C = m.shape[1]
+        phi, m = phi.contiguous(), m.contiguous()
+        D = torch.empty(20, N, C, dtype=phi.dtype, device=phi.device)
+        _lib.call("facek_cp_density_fwd", _tag(phi), _p(Y), _p(phi), phi.shape[1], r_off, _p(m), _p(gr["row_ptr"]), N,
+                  C, _p(D), _lib.stream())
+        ctx.save_for_backward(Y, phi, m)
+        ctx.r_off, ctx.gr = r_off, gr
+        return tuple(D[a:b] for a, b in RANK)
+
+    @staticmethod
+    def backward(ctx, *dD):
+        Y, phi, m = ctx.saved_tensors
+        gr = ctx.gr
+        N = gr["row_ptr"].numel() - 1
+        E, C = m.shape
+        G = torch.cat([g if g is not None else torch.zeros(b - a, N, C, dtype=phi.dtype, device=phi.device)
+                       for g, (a, b) in zip(dD, RANK)], 0).contiguous()
+        dphi = torch.zeros_like(phi)
+        dm, dY = torch.empty_like(m), torch.empty_like(Y)
+        _lib.call("facek_cp_density_bwd", _tag(phi), _p(Y), _p(phi), phi.shape[1], ctx.r_off, _p(m), _p(G),
+                  _p(gr["ei"]), _p(gr["row_ptr"]), N, E, C, _p(dphi), _p(dm), _p(dY), _lib.stream())
+        return dY, dphi, None, dm, None
+
+
+def moment_transport(phi, Y, Vt, Mt, gr, C):
+    """Rank-1 and rank-2 transport sums of the non-factorised block (face/model.py:188-201), per channel:
+    A1[:, i] = sum_e Rt0 V_j + Rt1 M_j u,  A2[:, i] = sum_e Rt2 M_j + Rt3 sym(u V_j), with Rt = phi[:, 4C:8C]
+    (envelope included) and V (3, N, C), M (6, N, C) the projected previous-pass tensors (symmetric storage
+    xx yy zz xy xz yz).  Written with torch gathers and index_add (this form is not on the benchmark path)."""
+    ei, ej = gr["ei"].long(), gr["ej"].long()
+    E = ei.numel()
+    N = gr["row_ptr"].numel() - 1
+    Rt = phi[:, 4 * C:8 * C].reshape(E, 4, C).transpose(0, 1)                        # (4, E, C)
+    u = Y[:, 1:4].t()[..., None]                                                      # (3, E, 1)
+    Vj, Mj = Vt[:, ej], Mt[:, ej]                                                     # (3|6, E, C)
+    xx, yy, zz, xy, xz, yz = Mj.unbind(0)
+    Mu = torch.stack([xx * u[0] + xy * u[1] + xz * u[2], xy * u[0] + yy * u[1] + yz * u[2],
+                      xz * u[0] + yz * u[1] + zz * u[2]])
+    uV = u * Vj
+    suv = torch.cat([uV, 0.5 * torch.stack([u[0] * Vj[1] + u[1] * Vj[0], u[0] * Vj[2] + u[2] * Vj[0],
+                                            u[1] * Vj[2] + u[2] * Vj[1]])], 0)
+    t1 = Rt[0] * Vj + Rt[1] * Mu                                                      # (3, E, C)
+    t2 = Rt[2] * Mj + Rt[3] * suv                                                     # (6, E, C)
+    A1 = torch.zeros(3, N, C, dtype=phi.dtype, device=phi.device).index_add(1, ei, t1)
+    A2 = torch.zeros(6, N, C, dtype=phi.dtype, device=phi.device).index_add(1, ei, t2)
+    return A1, A2
+
+
 class Transport(torch.autograd.Function):
     """Transport sums as two planes (3, N, 2*B*Kd) [V, M u] and (6, N, 2*B*Kd) [M, sym(u V)], Gt (9, N, Kd)."""
 
@@ -339,6 +396,72 @@ class CoulombReal(torch.autograd.Function):
         _lib.call("facek_coulomb_real_bwd", _tag(q), _p(vec), _p(ctx.gr["row_ptr"]), _p(ctx.gr["ej"]), _p(q),
                   ctx.gamma, ctx.gp, ctx.cut, _p(g_row), q.shape[0], _p(dvec), 0, _p(dq), _lib.stream())
         return dvec, dq, None, None, None
+
+
+class ZBLTerm(torch.autograd.Function):
+    """Per-atom ZBL energy e_row[i] = 1/2 sum_{e in row i} E_zbl(r_e; Z_i, Z_j) (face/model.py:544-554)."""
+
+    @staticmethod
+    def forward(ctx, vec, gr, Z32, r_in, r_out):
+        N = gr["row_ptr"].numel() - 1
+        e_row = torch.empty(N, dtype=vec.dtype, device=vec.device)
+        _lib.call("facek_zbl_fwd", _tag(vec), _p(vec), _p(gr["row_ptr"]), _p(gr["ej"]), _p(Z32), r_in, r_out, N,
+                  _p(e_row), _lib.stream())
+        ctx.save_for_backward(vec, Z32)
+        ctx.gr, ctx.r = gr, (r_in, r_out)
+        return e_row
+
+    @staticmethod
+    def backward(ctx, g_row):
+        vec, Z32 = ctx.saved_tensors
+        dvec = torch.empty_like(vec)
+        _lib.call("facek_zbl_bwd", _tag(vec), _p(vec), _p(ctx.gr["row_ptr"]), _p(ctx.gr["ej"]), _p(Z32), *ctx.r,
+                  _p(g_row.contiguous()), g_row.shape[0], _p(dvec), 0, _lib.stream())
+        return dvec, None, None, None, None
+
+
+class DispTerm(torch.autograd.Function):
+    """Per-atom dispersion energy over the long-range list (face/dispersion.py:36-48):
+    e_row[i] = sum_{e in row i} -1/2 sqrt(C6_i C6_j) / (d^6 + R0_ij^6) s(d)."""
+
+    @staticmethod
+    def forward(ctx, vec, C6, lr, r0, A, r_long):
+        N = lr["row_ptr"].numel() - 1
+        C6 = C6.contiguous()
+        e_row = torch.empty(N, dtype=vec.dtype, device=vec.device)
+        _lib.call("facek_disp_fwd", _tag(vec), _p(vec), _p(lr["row_ptr"]), _p(lr["ej"]), _p(C6), _p(r0), _p(A), r_long,
+                  N, _p(e_row), _lib.stream())
+        ctx.save_for_backward(vec, C6, r0, A)
+        ctx.lr, ctx.r_long = lr, r_long
+        return e_row
+
+    @staticmethod
+    def backward(ctx, g_row):
+        vec, C6, r0, A = ctx.saved_tensors
+        dvec, dC6 = torch.empty_like(vec), torch.empty_like(C6)
+        _lib.call("facek_disp_bwd", _tag(vec), _p(vec), _p(ctx.lr["row_ptr"]), _p(ctx.lr["ej"]), _p(C6), _p(r0),
+                  _p(A), ctx.r_long, _p(g_row.contiguous()), g_row.shape[0], _p(dvec), 0, _p(dC6), _lib.stream())
+        return dvec, dC6, None, None, None, None
+
+
+def zbl_term(P, gr, geo):
+    """ZBL over the model's neighbour list (face/model.py:544-554)."""
+    z = P["zbl"]
+    return ZBLTerm.apply(geo["vec"], gr, gr["Z"].to(torch.int32).contiguous(), z["r_in"], z["r_out"])
+
+
+def disp_term(P, gr, pos, h):
+    """Dispersion over the long-range list gr["lr"] (face/dispersion.py:36-48); C6_i = c6(Z_i) exp(w . h_i)."""
+    c = P["disp"]
+    lr = gr.get("lr")
+    if lr is None:
+        raise KeyError("the dispersion term needs a long-range pair list: build_graph(..., rc_long=...) or the "
+                       "reference graph keys lr_i / lr_j / lr_shift")
+    Z = gr["Z"]
+    C6 = c["c6"][Z] * torch.exp(_layer(c["w"], h).squeeze(-1))
+    r0 = c["r0"][Z].contiguous()
+    vec = EdgeVec.apply(pos, lr)
+    return DispTerm.apply(vec, C6, lr, r0, c["A"], c["r_long"])
 
 
 _BMOD = {}
@@ -532,14 +655,18 @@ def prepare(model, dtype, dev):
         q["pair"] = d(blk.pair.weight)
         q["w2"], q["b2"] = _lin(model, blk.radial[0], dtype, dev)
         q["w3"], q["b3"] = _lin(model, blk.radial[2], dtype, dev)
+        q["R"] = q["w3"].shape[0]
         sp = model.spline[t]
         q["spline"] = None if sp is None else (d(sp[0]), d(sp[1]), float(sp[2]))
-        q["msg_w"], q["msg_b"] = _lin(model, blk.msg, dtype, dev)
-        q["mixT"] = [(_lin(model, blk.mix[l], dtype, dev)[0]).t().contiguous() for l in range(4)]      # (BK, C)
-        q["projT"] = [(_lin(model, blk.proj[l], dtype, dev)[0]).t().contiguous() for l in range(4)]    # (cin, 3C)
+        q["form"] = blk.form
         tc = dtype == torch.float32 and torch.device(dev).type == "cuda"
         pk = (lambda W, b=None: Dense(W, b) if tc and Dense.ok(*W.shape) else None)
-        q["mixD"] = [pk(W) for W in q["mixT"]]
+        if blk.form != "moment":
+            q["msg_w"], q["msg_b"] = _lin(model, blk.msg, dtype, dev)
+            # (B*K, C) factorised, (C, C) CP
+            q["mixT"] = [(_lin(model, blk.mix[l], dtype, dev)[0]).t().contiguous() for l in range(4)]
+            q["mixD"] = [pk(W) for W in q["mixT"]]
+        q["projT"] = [(_lin(model, blk.proj[l], dtype, dev)[0]).t().contiguous() for l in range(4)]    # (cin, 3C)
         q["projD"] = [pk(W) for W in q["projT"]]
         q["elem_scale"] = d(blk.elem_scale.weight)
         q["norm"] = blk.norm_kind
@@ -557,18 +684,34 @@ def prepare(model, dtype, dev):
             wd, bd = _lin(model, blk.dir_mix, dtype, dev)                                 # (K, 4Kd)
             q["dir"] = [wd[:, i * Kd:(i + 1) * Kd].t().contiguous() for i in range(4)]       # each (Kd, K)
             q["dir_b"] = bd
-            q["pvtT"] = _lin(model, blk.pvt, dtype, dev)[0].t().contiguous()                # (cprev, nt*Kd)
-            q["pmtT"] = _lin(model, blk.pmt, dtype, dev)[0].t().contiguous()
+            if blk.form == "moment":                      # face/model.py:147-150: pv, pm (cprev -> Kd)
+                q["pvtT"] = _lin(model, blk.pv, dtype, dev)[0].t().contiguous()             # (cprev, Kd)
+                q["pmtT"] = _lin(model, blk.pm, dtype, dev)[0].t().contiguous()
+            else:
+                q["pvtT"] = _lin(model, blk.pvt, dtype, dev)[0].t().contiguous()            # (cprev, nt*Kd)
+                q["pmtT"] = _lin(model, blk.pmt, dtype, dev)[0].t().contiguous()
             q["y2w"] = torch.tensor(Y2W, dtype=dtype, device=dev)[:, None, None]
             # the y2 weights folded into per-component maps: (Md @ w) * y2w == Md @ (w * y2w), one batched matmul
             q["dir_y2"] = [q["y2w"] * q["dir"][i] for i in (1, 3)]                            # each (6, Kd, K)
-        if blk.transport:
+        if blk.transport and blk.form == "moment":        # face/model.py:151-153: tv, tm (cprev -> C)
+            q["tvT"] = _lin(model, blk.tv, dtype, dev)[0].t().contiguous()
+            q["tmT"] = _lin(model, blk.tm, dtype, dev)[0].t().contiguous()
+        elif blk.transport:
             for name in ("tmix1", "tmix2"):
                 w = _lin(model, getattr(blk, name), dtype, dev)[0]                           # (C, B*2*Kd) cols (b,t,kd)
                 q[name + "T"] = w.view(C, B, 2, Kd).permute(0, 2, 1, 3).reshape(C, 2 * B * Kd).t().contiguous()
                 q[name + "D"] = pk(q[name + "T"])
         blocks.append(q)
     P["blocks"] = blocks
+    P["terms"] = list(model.terms.keys())
+    if "zbl" in model.terms:
+        tm = model.terms["zbl"]
+        P["zbl"] = {"r_in": float(tm.r_in), "r_out": float(tm.r_out)}
+    if "disp" in model.terms:
+        tm = model.terms["disp"]
+        P["disp"] = {"w": _lin(model, tm.w, dtype, dev), "c6": d(tm.c6), "r0": d(tm.r0), "r_long": float(tm.r_long),
+                     # softplus(a1), softplus(a2) of face/dispersion.py:44, kept on the device (no host read)
+                     "A": F.softplus(torch.stack([tm.a1.detach(), tm.a2.detach()])).to(dtype=dtype, device=dev)}
     if "coulomb" in model.terms:
         tm = model.terms["coulomb"]
         P["coulomb"] = {"h0": _lin(model, tm.head[0], dtype, dev), "h2": _lin(model, tm.head[2], dtype, dev),
@@ -606,13 +749,61 @@ def _layer(W, x):
     return F.linear(x, w, b)
 
 
+def channel_moments(q, gr, geo, h, A_sets, eq, phi):
+    """Moments of the CP form and of the non-factorised block (face/model.py:496-502 with :533-534; :160-201): the
+    per-channel edge message (h_j or msg(h)_j, plus the directional term as per-atom tables), the per-channel
+    density, the C -> C channel map (CP only) and the transport increments, before the element scaling."""
+    N, C, B, Kd = h.shape[0], q["C"], q["B"], q["Kd"]
+    vec, Y = geo["vec"], geo["Y"]
+    cp = q["form"] == "cp"
+    base = F.linear(h, q["msg_w"], q["msg_b"]) if cp else h                        # (N, C)
+    Gt = tsrc = None
+    if q["directional"]:
+        src1 = eq[0] if q["eq_in"] else torch.cat([A[1] for A in A_sets], 2)        # (3, N, cprev)
+        src2 = eq[1] if q["eq_in"] else torch.cat([A[2] for A in A_sets], 2)        # (6, N, cprev)
+        Vb = src1 @ q["pvtT"]
+        Mb = src2 @ q["pmtT"]
+        Vd, Md = Vb[..., :Kd], Mb[..., :Kd]
+        w1, w2, w3, w4 = q["dir"]
+        w2y, w4y = q["dir_y2"]
+        TJ = torch.cat([(base + q["dir_b"])[None], Vd @ w1, Md @ w2y], 0)            # (10, N, C)
+        TI = torch.cat([torch.zeros_like(base)[None], Vd @ w3, Md @ w4y], 0)
+        m = EdgeMsg.apply(Y, TJ, TI, gr)                                               # (E, C)
+        if q["transport"]:
+            if cp:
+                Gt = torch.cat([Vb[..., Kd:], Mb[..., Kd:]], 0)                        # (9, N, Kd)
+            else:
+                tsrc = (src1 @ q["tvT"], src2 @ q["tmT"])                              # (3|6, N, C)
+    else:
+        m = EdgeMsg.apply(Y, base[None], None, gr)
+    D = CPDensity.apply(Y, phi, B if cp else 0, m, gr)                                # 4 x (k_l, N, C)
+    if cp:
+        tpl = {}
+        if Gt is not None:
+            T1, T2 = Transport.apply(phi[:, :B].contiguous(), vec, Gt, gr)
+            tpl = {1: (T1, q["tmix1T"], q["tmix1D"]), 2: (T2, q["tmix2T"], q["tmix2D"])}
+        return [mm(D[l], q["mixT"][l], q["mixD"][l], *tpl.get(l, (None, None, None))) for l in range(4)]
+    A = list(D)
+    if tsrc is not None:
+        A1, A2 = moment_transport(phi, Y, tsrc[0], tsrc[1], gr, C)
+        A[1] = A[1] + A1
+        A[2] = A[2] + A2
+    return A
+
+
 def block_forward(P, t, gr, geo, h, A_sets, eq):
-    """One factorised pass (face/model.py:310-339 with FactorBlock.moments :460-534)."""
+    """One interaction pass (face/model.py:310-339 with FactorBlock.moments :460-534, or the CP form and the
+    non-factorised MomentBlock.moments :160-201)."""
     q = P["blocks"][t]
     N = h.shape[0]
     C, B, K, Kd = q["C"], q["B"], q["K"], q["Kd"]
     vec, Y = geo["vec"], geo["Y"]
     phi = Radial.apply(vec, gr, q)                                                   # (E, B), env included
+    s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1).contiguous()   # (4, N, C)
+    if q["form"] != "factor":
+        A = channel_moments(q, gr, geo, h, A_sets, eq, phi)
+        A = [BcastMul.apply(A[l], s[l]) for l in range(4)]
+        return _invariants_readout(P, q, h, A_sets, A, N)
     msgtab = F.linear(h, q["msg_w"], q["msg_b"])                                     # (N, K)
     Gt = None
     if q["directional"]:
@@ -630,13 +821,17 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
         D = DensityMsg.apply(phi, Y, TJ, TI, gr)                                     # 4 x (k_l, N, B*K)
     else:
         D = DensityMsg.apply(phi, Y, msgtab[None], None, gr)
-    s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1).contiguous()   # (4, N, C)
     tpl = {}
     if Gt is not None:
         T1, T2 = Transport.apply(phi, vec, Gt, gr)                                   # (3|6, N, 2*B*Kd)
         tpl = {1: (T1, q["tmix1T"], q["tmix1D"]), 2: (T2, q["tmix2T"], q["tmix2D"])}
     A = [mm(D[l], q["mixT"][l], q["mixD"][l], *tpl.get(l, (None, None, None))) for l in range(4)]   # (k_l, N, C)
     A = [BcastMul.apply(A[l], s[l]) for l in range(4)]
+    return _invariants_readout(P, q, h, A_sets, A, N)
+
+
+def _invariants_readout(P, q, h, A_sets, A, N):
+    """Invariants, norm, readout and gated equivariant outputs of a pass (face/model.py:204-339)."""
     # invariants (face/model.py:204-270): projections straight into the node kernel's layout
     sets = A_sets + [A]
     ys = [mm(torch.cat([a[l] for a in sets], 2), q["projT"][l], q["projD"][l]) for l in range(4)]   # (k_l, N, 3C)
@@ -764,8 +959,15 @@ def face_forward(model, g, forces=True):
     with torch.set_grad_enabled(forces):
         e_at, h, P, gr, geo = local_energies(model, gr, pos)
         qv = None
-        if "coulomb" in P:
-            ea, qv = coulomb_term(P, gr, geo, h, pos)
+        for name in P["terms"]:                          # face/model.py:686-687, in the model's term order
+            if name == "coulomb":
+                ea, qv = coulomb_term(P, gr, geo, h, pos)
+            elif name == "zbl":
+                ea = zbl_term(P, gr, geo)
+            elif name == "disp":
+                ea = disp_term(P, gr, pos, h)
+            else:
+                raise NotImplementedError(name)
             e_at = e_at + ea
         E = seg_sum(e_at, gr["batch"], gr["nstr"])
         out = {"energy": E.detach(), "atom_energy": e_at.detach()}

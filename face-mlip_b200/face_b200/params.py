@@ -14,7 +14,8 @@ import numpy as np
 import torch
 import torch.nn as nn
 
-LINEAR_NAMES = ("rad_in", "radial.0", "radial.2", "msg", "dir_mix", "pvt", "pmt", "tmix1", "tmix2", "tmix3",
+LINEAR_NAMES = ("rad_in", "radial.0", "radial.2", "msg", "dir_mix", "pvt", "pmt", "pv", "pm", "tv", "tm", "tmix1",
+                "tmix2", "tmix3",
                 "gate", "head.0", "head.2") + tuple(f"mix.{l}" for l in range(4)) + tuple(
     f"proj.{l}" for l in range(4)) + ("out.0", "out.2", "out.4")
 
@@ -41,11 +42,20 @@ class Affine(nn.Module):
 
 
 class BlockParams(nn.Module):
-    """Parameters of one factorised interaction pass (no compute here; see face_b200.model)."""
+    """Parameters of one interaction pass (no compute here; see face_b200.model), in one of three forms:
+      "factor"  FactorBlock, B radials x K-channel messages (face/model.py:421-458)
+      "cp"      FactorBlock with cp=True: per-channel messages (K = C), B + 4C radials, C -> C channel maps
+                (face/model.py:436-449)
+      "moment"  the non-factorised MomentBlock: 4C (8C with transport) radials, neighbour features h_j as the
+                message, no channel map, per-channel transport maps tv / tm (face/model.py:99-158)"""
     N_INV = 9
 
-    def __init__(self, C, n_basis, n_sets, radial_hidden, n_el, K_dir, norm, transport, eq_in, eq_out, B, K):
+    def __init__(self, C, n_basis, n_sets, radial_hidden, n_el, K_dir, norm, transport, eq_in, eq_out, B, K,
+                 form="factor"):
         super().__init__()
+        self.form = form
+        if form == "cp":
+            K = C
         self.C, self.B, self.Km, self.Kd, self.n_el = C, B, K, K_dir, n_el
         self.eq_in, self.eq_out = eq_in, eq_out
         self.directional = n_sets > 1
@@ -72,12 +82,22 @@ class BlockParams(nn.Module):
             self.vpath = nn.Parameter(torch.ones(4, C))
             self.mpath = nn.Parameter(torch.ones(4, C))
             self.gate = nn.Linear(self.N_INV * C, 2 * C)
-        self.radial = _mlp([radial_hidden, radial_hidden, B])
+        cprev = C if eq_in else C * (n_sets - 1)
+        if form == "moment":
+            self.radial = _mlp([radial_hidden, radial_hidden, (8 if self.transport else 4) * C])
+            if self.directional:
+                self.pv = nn.Linear(cprev, K_dir, bias=False)
+                self.pm = nn.Linear(cprev, K_dir, bias=False)
+                self.dir_mix = nn.Linear(4 * K_dir, C)
+            if self.transport:
+                self.tv = nn.Linear(cprev, C, bias=False)
+                self.tm = nn.Linear(cprev, C, bias=False)
+            return
+        self.radial = _mlp([radial_hidden, radial_hidden, B + (4 * C if form == "cp" else 0)])
         self.msg = nn.Linear(C, K)
-        self.mix = nn.ModuleList([nn.Linear(B * K, C, bias=False) for _ in range(4)])
+        self.mix = nn.ModuleList([nn.Linear(C if form == "cp" else B * K, C, bias=False) for _ in range(4)])
         if self.directional:
             self.dir_mix = nn.Linear(4 * K_dir, K)
-            cprev = C if eq_in else C * (n_sets - 1)
             nt = 2 if self.transport else 1
             self.pvt = nn.Linear(cprev, nt * K_dir, bias=False)
             self.pmt = nn.Linear(cprev, nt * K_dir, bias=False)
@@ -97,6 +117,42 @@ class ChargeParams(nn.Module):
         self.gp = max(rc_real / acc, 1.05 * self.gamma)
         self.kcut = 2 * acc / self.gp
         self.mesh = None            # None -> face-mlip's rule n = max(8, ceil(L / (gp/4)))
+
+
+class ZBLParams(nn.Module):
+    """The ZBL term (face/model.py:538-541): no parameters, inner and outer switching radii."""
+
+    def __init__(self, r_in=0.6, r_out=1.2):
+        super().__init__()
+        self.r_in, self.r_out = r_in, r_out
+
+
+# Tkatchenko-Scheffler free-atom C6 (Hartree Bohr^6) and vdW radii (Bohr), the published values the reference's
+# dispersion term tabulates (face/dispersion.py:16-19); elements without an entry take carbon's.
+_TS_C6 = {1: 6.50, 6: 46.6, 7: 24.2, 8: 15.6, 11: 1556.0, 12: 627.0, 13: 528.0, 17: 94.6, 47: 339.0, 79: 298.0}
+_TS_R0 = {1: 3.10, 6: 3.59, 7: 3.34, 8: 3.19, 11: 3.74, 12: 3.66, 13: 3.84, 17: 3.71, 47: 3.82, 79: 3.86}
+_HARTREE_EV, _BOHR_A = 27.211386, 0.529177
+
+
+class DispParams(nn.Module):
+    """Dispersion term parameters (face/dispersion.py:22-34): w (C -> 1) modulating the free-atom C6 by the
+    environment, Becke-Johnson damping a1/a2, per-element C6 (eV A^6) and radii (A) buffers over Z = 0..118."""
+
+    def __init__(self, C, r_long=10.0):
+        super().__init__()
+        self.r_long = r_long
+        self.w = nn.Linear(C, 1)
+        self.a1 = nn.Parameter(torch.tensor(0.4))
+        self.a2 = nn.Parameter(torch.tensor(2.5))
+        unit = _HARTREE_EV * _BOHR_A ** 6
+        c6 = torch.full((119,), _TS_C6[6] * unit)
+        r0 = torch.full((119,), _TS_R0[6] * _BOHR_A)
+        for z, v in _TS_C6.items():
+            c6[z] = v * unit
+        for z, v in _TS_R0.items():
+            r0[z] = v * _BOHR_A
+        self.register_buffer("c6", c6)
+        self.register_buffer("r0", r0)
 
 
 def _fan_in(model, name):
@@ -122,6 +178,10 @@ def seeded_state(model, seed, perturb=0.25):
         is_lin = last in LINEAR_NAMES or two in LINEAR_NAMES
         if last == "gate":                                  # face/model.py:158
             base = np.zeros(sh) if leaf == "weight" else np.ones(sh)
+        elif last == "disp" and leaf in ("a1", "a2"):     # face/dispersion.py:27
+            base = np.full(sh, 0.4 if leaf == "a1" else 2.5)
+        elif mod.endswith("disp.w"):                       # face/dispersion.py:26: zero-initialised modulation
+            base = np.zeros(sh)
         elif is_lin and leaf == "weight":
             bound = 1.0 if unit else _fan_in(model, name) ** -0.5
             base = rng.uniform(-bound, bound, sh)

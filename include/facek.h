@@ -167,7 +167,9 @@ int facek_radial_fwd(int dtype, const void* vec, const int32_t* ei, const int32_
                      int32_t n_el, double rc, int32_t nb, int32_t H, int32_t B, const void* w1, const void* b1,
                      const void* pair, const void* w2, const void* b2, const void* w3, const void* b3, void* phi,
                      void* dphidr, int64_t E, void* stream);
-/* facek_radial_fwd runs fp32 with H = 64, B in {16, 32}, nb <= 16 on the tcgen05 tensor cores (fp32 accuracy through
+/* Wide outputs (B > 32: the CP form's B + 4C radials, face/model.py:449; the non-factorised block's 4C or 8C,
+ * face/model.py:130) run a CUDA-core kernel that keeps both hidden layers in registers.
+ * facek_radial_fwd runs fp32 with H = 64, B in {16, 32}, nb <= 16 on the tcgen05 tensor cores (fp32 accuracy through
  * the 3-term tf32 split); fp64 and other shapes on the CUDA cores. The two explicit variants below pick one path;
  * they have no reference counterpart (the reference has a single PyTorch path, face/model.py:465-469) and exist so
  * that callers and tests can compare the paths. facek_radial_tc_fwd is fp32 only and returns FACEK_EINVAL for
@@ -250,6 +252,42 @@ int facek_coulomb_real_fwd(int dtype, const void* vec, const int32_t* row_ptr, c
 int facek_coulomb_real_bwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej, const void* q,
                            double gamma, double gp, double r_cut, const void* g_row, int64_t N, void* dvec,
                            int32_t accumulate, void* dq, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Per-channel Cartesian density of the CP form (face/model.py:496-502, FactorBlock cp=True) and of the
+ * non-factorised MomentBlock (face/model.py:160-187): D[x, i, c] = sum_{e in row i} Y[e,x] R[e, l(x), c] m[e, c],
+ * D component-major (20, N, C).  R: per-(rank, channel) radial functions, envelope included, at column r_off of rows
+ * of stride ldr (the radial output row: CP keeps its B transport radials in columns 0..B-1); m (E, C) the edge
+ * message.  The adjoint takes G = dL/dD and writes dR at the same columns (other columns untouched), dm and dY.
+ */
+int facek_cp_density_fwd(int dtype, const void* Y, const void* R, int64_t ldr, int32_t r_off, const void* m,
+                         const int32_t* row_ptr, int64_t N, int32_t C, void* D, void* stream);
+int facek_cp_density_bwd(int dtype, const void* Y, const void* R, int64_t ldr, int32_t r_off, const void* m,
+                         const void* G, const int32_t* ei, const int32_t* row_ptr, int64_t N, int64_t E, int32_t C,
+                         void* dR, void* dm, void* dY, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
+ * Pair physics terms, per CSR row over a symmetric neighbour list (vec from facek_edge_vec of that list).
+ * ZBL (face/model.py:538-554, the "zbl" term): e_row[i] = 1/2 sum_{e in row i} KE Zi Zj / r phi(r/a) s(r),
+ *   a = 0.46850 / (Zi^0.23 + Zj^0.23), phi the universal 4-exponential screening, s the quintic switch from 1 at
+ *   r_in to 0 at r_out (reference r_in = 0.6, r_out = 1.2 A); Z = atomic numbers (int32).  The adjoint writes
+ *   dvec[e] (+)= g_row[i] / 2 dE/dr u for the row's own edges.
+ * Dispersion (face/dispersion.py:36-48, the "disp" term) over the long-range pair list (face/datasets.py:53-55):
+ *   e_row[i] = sum_{e in row i} -1/2 sqrt(C6_i C6_j) / (d^6 + R0^6) s(d), R0 = A[0] (r0_i + r0_j)/2 + A[1]
+ *   (A = softplus of the learned a1, a2, on the device), s the quintic switch from 1 at r_long - 2 to 0 at r_long.
+ *   C6 (N) is the environment-modulated per-atom coefficient and r0 (N) the per-atom vdW radius.  The adjoint
+ *   writes dvec[e] (+)= g_row[i] de/dd u and dC6[i] = sum_{e in row i} (g_i + g_j) e_ij / (2 C6_i).
+ */
+int facek_zbl_fwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej, const int32_t* Z,
+                  double r_in, double r_out, int64_t N, void* e_row, void* stream);
+int facek_zbl_bwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej, const int32_t* Z,
+                  double r_in, double r_out, const void* g_row, int64_t N, void* dvec, int32_t accumulate,
+                  void* stream);
+int facek_disp_fwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej, const void* C6,
+                   const void* r0, const void* A, double r_long, int64_t N, void* e_row, void* stream);
+int facek_disp_bwd(int dtype, const void* vec, const int32_t* row_ptr, const int32_t* ej, const void* C6,
+                   const void* r0, const void* A, double r_long, const void* g_row, int64_t N, void* dvec,
+                   int32_t accumulate, void* dC6, void* stream);
 
 #ifdef __cplusplus
 }

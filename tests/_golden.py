@@ -10,7 +10,12 @@ GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 SMALL_CASES = ["cfg1", "cfg1_spline", "cfg2", "cfg3_small", "cfg4_small", "cfg5_small"]
 # the benchmark configurations at full size (cfg3: 15,590 atoms; cfg4: 32,768 atoms) and a 37,044-atom cfg5 sub-box
 FULL_CASES = ["cfg3", "cfg4", "cfg5_37k"]
-MODEL_CASES = SMALL_CASES + FULL_CASES
+# physics terms: ZBL and dispersion (the latter needs the 10 A long-range list, rc_long below)
+TERM_CASES = ["zbl_mol", "disp_mol", "disp_nacl"]
+RC_LONG = 10.0
+# the CP form and the non-factorised MomentBlock
+FORM_CASES = ["cp_small", "cp_mol", "cp_spline", "moment_small", "moment_mol"]
+MODEL_CASES = SMALL_CASES + FULL_CASES + TERM_CASES + FORM_CASES
 
 
 def load(name):

@@ -41,6 +41,24 @@ CASES = [
     ("cfg4", 4, None, {}, (96, 96, 96), False),
     ("cfg5_37k", 5, 21, {}, (84, 84, 84), False),
 ]
+# physics terms (face/model.py:538-590): ZBL on molecules (close contacts below the 1.2 A switch), dispersion over the
+# 10 A long-range list on molecules and on a periodic rock-salt box together with the PME Coulomb term
+TERM_CASES = [
+    ("zbl_mol", 3, 6, {"terms": ("zbl",)}, None, False),
+    ("disp_mol", 3, 6, {"terms": ("disp",)}, None, False),
+    ("disp_nacl", 2, 2, {"terms": ("coulomb", "disp")}, (20, 20, 20), False),
+]
+# the other density forms of the shipped checkpoints (face/model.py:99-202, :421-534): the CP form (cp=True, per-channel
+# messages) and the non-factorised MomentBlock (factor=False), both with transport and equivariant messages
+FORM_CASES = [
+    ("cp_small", 5, 4, {"cp": True}, (24, 24, 24), False),
+    ("cp_mol", 3, 6, {"cp": True, "C": 32}, None, False),
+    ("cp_spline", 1, None, {"cp": True}, None, True),
+    ("moment_small", 5, 4, {"factor": False}, (24, 24, 24), False),
+    ("moment_mol", 3, 6, {"factor": False, "C": 32}, None, False),
+]
+CASES += TERM_CASES + FORM_CASES
+R_LONG = 10.0       # the dispersion term's default r_long, also the long-range list cutoff here
 BIG = 4000          # cases above this many atoms store a position hash instead of the positions
 
 
@@ -77,6 +95,7 @@ def run_model_case(ref, name, cfg, scale, over, mesh, spline, seed=0):
         pme["mesh"] = mesh
     rc = systems.MODELS[cfg]["rc"]
     g = nlist.padded_graph(structs, rc)
+    lr = long_range_pairs(structs, R_LONG) if "disp" in systems.model_kwargs(cfg, **over)["terms"] else None
     out = {}
     orig = fe.pme_recip_energy
     for dt, tag in ((torch.float64, "64"), (torch.float32, "32")):
@@ -97,6 +116,8 @@ def run_model_case(ref, name, cfg, scale, over, mesh, spline, seed=0):
               "shift": torch.tensor(g["shift"], dtype=dt), "mask": torch.tensor(g["mask"]),
               "batch": torch.tensor(g["batch"]), "cell": torch.tensor(g["cell"], dtype=dt),
               "charge": torch.tensor(g["charge"], dtype=dt), "nstr": int(g["nstr"])}
+        if lr is not None:
+            gg.update(lr_i=torch.tensor(lr[0]), lr_j=torch.tensor(lr[1]), lr_shift=torch.tensor(lr[2], dtype=dt))
         o = m(gg)
         fe.pme_recip_energy = orig
         out["energy" + tag] = o["energy"].detach().double().numpy()
@@ -123,6 +144,19 @@ def run_model_case(ref, name, cfg, scale, over, mesh, spline, seed=0):
                         **out)
     print(f"{name}: N={len(g['pos'])} E={len(edges)} M={g['nbr'].shape[1]}  E64={out['energy64'][:3]}  "
           f"|F|max={np.abs(out['forces64']).max():.3e}  dE32/E={np.abs(out['energy32'] - out['energy64']).max() / np.abs(out['energy64']).max():.1e}")
+
+
+def long_range_pairs(structs, r_long):
+    """GraphSet's long-range list (face/datasets.py:53-55, 90-95): (i, j, S @ cell) of every structure, offset."""
+    I, J, SH, off = [], [], [], 0
+    for st in structs:
+        pbc = bool(np.any(st.pbc))
+        i, j, S = nlist.neighbor_list_ijS(st.positions, st.cell, pbc, r_long)
+        I.append(i + off)
+        J.append(j + off)
+        SH.append(nlist.shift_vectors(S, np.asarray(st.cell, np.float64)) if pbc else np.zeros((len(i), 3)))
+        off += len(st.numbers)
+    return np.concatenate(I), np.concatenate(J), np.concatenate(SH)
 
 
 def _hash(edges):

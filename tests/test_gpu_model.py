@@ -8,7 +8,7 @@ import numpy as np
 import pytest
 import torch
 
-from _golden import MODEL_CASES, case_inputs
+from _golden import MODEL_CASES, RC_LONG, case_inputs
 
 pytestmark = pytest.mark.gpu
 if not torch.cuda.is_available():
@@ -34,7 +34,7 @@ def _run(name, dtype):
     from face_b200.neighbors import build_graph
     structs, spec, pme, d = case_inputs(name)
     m = _engine(spec, d["meta"]["seed"], pme, dtype, d["meta"]["spline"])
-    g = build_graph(structs, spec["rc"], dtype=dtype)
+    g = build_graph(structs, spec["rc"], dtype=dtype, rc_long=RC_LONG if "disp" in spec.get("terms", ()) else None)
     o = m(g)
     return o, d
 
@@ -66,17 +66,23 @@ def test_fp32_matches_reference(name):
     """fp32 bars: energy within 1e-6 relative, forces within 1e-4 eV/A.  Model cases are held to both the reference's
     fp64 and fp32 outputs.  The compiled-radial case is held to the reference's fp32 outputs: its Hermite tables are
     built in the model's precision (face/model.py:393-405), so the fp32 spline is a different function from the fp64
-    one at the 1e-7 level of the table entries."""
+    one at the 1e-7 level of the table entries.  Where the reference's own fp32 result misses its fp64 result by more
+    than these bars (the ZBL case: close contacts with forces near 90 eV/A), the bar is twice the reference's own fp32
+    deviation."""
     o, d = _run(name, torch.float32)
     E, F = o["energy"].double().cpu().numpy(), o["forces"].double().cpu().numpy()
     scale = np.abs(d["energy64"]).max()
+    gap_e = np.abs(d["energy32"] - d["energy64"]).max()
+    gap_f = np.abs(d["forces32"] - d["forces64"]).max()
+    tol_e = max(1e-6 * scale, 2 * gap_e)
+    tol_f = max(1e-4, 2 * gap_f)
     refs = [("32", d["energy32"], d["forces32"])]
     if not d["meta"]["spline"]:
         refs.append(("64", d["energy64"], d["forces64"]))
     for tag, Er, Fr in refs:
-        assert np.abs(E - Er).max() <= 1e-6 * scale, (tag, E, Er)
+        assert np.abs(E - Er).max() <= tol_e, (tag, E, Er, tol_e)
         dF = np.abs(F - Fr).max()
-        assert dF <= 1e-4 and dF <= 1e-4 * max(1.0, np.abs(Fr).max()), (tag, dF)
+        assert dF <= tol_f, (tag, dF, tol_f)
 
 
 def test_reference_padded_graph_input():

@@ -5,7 +5,7 @@ import numpy as np
 import pytest
 import torch
 
-from _golden import SMALL_CASES, case_inputs, load
+from _golden import RC_LONG, SMALL_CASES, TERM_CASES, case_inputs, load
 from oracle import face_ref, nlist
 
 
@@ -18,10 +18,24 @@ def _engine_state(spec, seed):
     return m.seed_(seed).state_dict()
 
 
-@pytest.mark.parametrize("name", SMALL_CASES)
+def _long_range(structs, r_long):
+    I, J, SH, off = [], [], [], 0
+    for st in structs:
+        pbc = bool(np.any(st.pbc))
+        i, j, S = nlist.neighbor_list_ijS(st.positions, st.cell, pbc, r_long)
+        I.append(i + off)
+        J.append(j + off)
+        SH.append(nlist.shift_vectors(S, np.asarray(st.cell, np.float64)) if pbc else np.zeros((len(i), 3)))
+        off += len(st.numbers)
+    return {"lr_i": np.concatenate(I), "lr_j": np.concatenate(J), "lr_shift": np.concatenate(SH)}
+
+
+@pytest.mark.parametrize("name", SMALL_CASES + TERM_CASES)
 def test_oracle_matches_reference(name):
     structs, spec, pme, d = case_inputs(name)
     g = nlist.padded_graph(structs, spec["rc"])
+    if "disp" in spec.get("terms", ()):
+        g.update(_long_range(structs, RC_LONG))
     ei = np.repeat(np.arange(len(g["nbr"])), g["mask"].sum(1))
     edges = np.concatenate([ei[:, None], g["nbr"][g["mask"]][:, None], g["S"][g["mask"]]], 1).astype(np.int64)
     assert hashlib.sha256(np.ascontiguousarray(edges).tobytes()).hexdigest() == str(d["edge_hash"])
