@@ -277,8 +277,6 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=12.0)
     ap.add_argument("--scale", type=int, default=None,
                     help="smaller system of the same configuration (cfg5: conventional cells per side), for profiling")
-    ap.add_argument("--pme", default="replicated", choices=["replicated", "slab"],
-                    help="N>1 periodic systems: PME mesh on every rank, or in x-slabs with an all-to-all FFT transpose")
     a = ap.parse_args()
     if a.impl == "reference":
         run_reference(a)

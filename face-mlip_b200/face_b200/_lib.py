@@ -62,6 +62,10 @@ SIGNATURES = {
     "facek_pme_gather": [I32, P, P, I64, PD, I32, I32, I32, P, D, P, P, P],
     "facek_cp_density_fwd": [I32, P, P, I64, I32, P, P, I64, I32, P, P],
     "facek_cp_density_bwd": [I32, P, P, I64, I32, P, P, P, P, I64, I64, I32, P, P, P, P],
+    "facek_layer_norm_fwd": [I32, P, P, P, D, I64, I32, P, P, P, P],
+    "facek_layer_norm_bwd": [I32, P, P, P, P, P, I64, I32, P, P],
+    "facek_silu_fwd": [I32, P, P, I64, P],
+    "facek_silu_bwd": [I32, P, P, P, I64, P],
     "facek_zbl_fwd": [I32, P, P, P, P, D, D, I64, P, P],
     "facek_zbl_bwd": [I32, P, P, P, P, D, D, P, I64, P, I32, P],
     "facek_disp_fwd": [I32, P, P, P, P, P, P, D, I64, P, P],

@@ -1,20 +1,26 @@
-"""Multi-GPU evaluation: spatial decomposition of a periodic system, one process per GPU.
+"""Multi-GPU evaluation: spatial decomposition of a periodic system with a per-pass halo exchange, one process per
+GPU; batches of independent molecules sharded by structure.
 
-The box (orthorhombic) is split into a grid of bricks (2x1x1, 2x2x1, 2x2x2, ...), one per rank.  A rank holds the
-atoms of its brick ("owned") plus every atom within `halo` = n_passes * rc of the brick along the split axes
-("ghosts", placed at the periodic image nearest the brick).  With that depth every owned atom's energy is computed
-exactly on the rank; ghosts only feed them.  Along unsplit axes the local system keeps the full periodicity, and the
-local extent along split axes stays below L - rc, so the local neighbour list is built with the original cell.
+Periodic systems.  The box (orthorhombic) is split into a grid of bricks (2x1x1, 2x2x1, 2x2x2, ...), one per rank.
+A rank owns the atoms of its brick and holds, as ghosts, every atom within rc of the brick along the split axes (at
+the periodic image nearest the brick).  Along unsplit axes the local system keeps the full periodicity, and the
+local extent along split axes stays below L - rc, so the local neighbour list is the ordinary periodic build with
+the original cell.  Coupling, all through one differentiable halo exchange (HaloExchange: an all-to-all of the
+ghost rows from their owners forward, and of the ghost gradients back to the owners, summed into the owned rows):
 
-Cross-rank coupling, all through differentiable collectives (torch.distributed.nn):
-  * latent-charge neutrality: mu = (Q + sum chi/J) / sum 1/J over all atoms -> two all-reduced sums
-    (face-mlip face/electrostatics.py:165-167);
-  * charges: the owned charges of all ranks are all-gathered into the global charge vector, which feeds the
-    real-space term of the owned rows and the PME reciprocal sum (computed redundantly on every rank on the full
-    mesh and counted once, 1/world per rank);
-  * forces: every rank differentiates its own energy (owned atoms + its share of the global terms) with respect to
-    the global positions; one all-reduce (sum) of that gradient gives the forces.
-Batches of non-periodic structures (molecules) are instead sharded by structure with no data-path collective.
+  * positions: each rank holds only its owned atoms' coordinates; ghost coordinates come from their owners (plus the
+    periodic image shift), and the gradient with respect to a ghost's coordinates goes back to its owner, which is
+    the reverse sum of ghost forces: no global position array and no N x 3 all-reduce;
+  * pass features: after every pass but the last, the ghosts' features that the next pass reads at a neighbour
+    (h, and the equivariant tensors V, M or the previous moment sets) are replaced by their owners' values, so the
+    next pass of every owned atom is exact although the ghost shell is only rc deep (face-mlip face/model.py:479-483
+    makes exactly these per-atom quantities available to the neighbour messages);
+  * latent charges: the two neutrality sums are all-reduced scalars (face/electrostatics.py:165-167), the charges of
+    ghosts come through the halo exchange for the real-space rows, and the PME reciprocal sum is mesh-distributed
+    (SlabPME: each rank spreads its owned charges, reduce-scatter into x-slabs, 2-D FFT, all-to-all transpose, 1-D
+    FFT);
+  * energy: one all-reduced scalar.
+Every rank runs the same collectives in the same order, forward and backward.
 """
 import json
 import math
@@ -88,54 +94,138 @@ class LocalSystem:
         self.charge = 0.0
 
 
-def rank_energy(pos_global, gid, img, owned, local_model, coulomb=None, world=1, group=None):
-    """This rank's share of the total energy as a differentiable function of the global positions.
+def brick_of(pos, L, grid):
+    """Owning rank (row-major over the grid) of every atom, from its wrapped position."""
+    Lt = torch.as_tensor(L, dtype=torch.float64, device=pos.device)
+    fw = torch.remainder(pos.double() / Lt, 1.0)
+    n = torch.as_tensor(grid, device=pos.device)
+    b = torch.clamp((fw * n).long(), max=n - 1)
+    return (b[:, 0] * grid[1] + b[:, 1]) * grid[2] + b[:, 2]
 
-    local_model(pos_local) -> (e_at, h): per-atom model energies and final features of the local atoms.
-    coulomb (optional): dict with
-        head(h) -> (chi, J);  real_rows(pos_local, q_local) -> e_row;  pme(pos_global, q_global) -> scalar;
-        optionally pme_slab(pos_owned, q_owned) -> this rank's share of the reciprocal energy (SlabPME);  gp, volume, charge (total charge Q), n_global, gid_owned_all (global ids of every rank's owned atoms in
-        all-gather order, padded with -1), max_owned.
+
+class HaloPlan:
+    """One rank's owned atoms, rc-deep ghosts and the exchange lists of the halo.
+
+    Local order: owned atoms (ascending global id), then ghosts grouped by owner rank (ascending), ascending global id
+    within an owner, so the all-to-all's receive buffer is the ghost block as is.  send_idx lists, peer by peer, the
+    owned rows that are ghosts on that peer, in the peer's order.  Built once from the global positions (every rank
+    derives every rank's ghost set with the same deterministic selection, so no index lists are exchanged)."""
+
+    def __init__(self, pos, L, grid, rank, world, halo, group=None):
+        self.rank, self.world, self.group = rank, world, group
+        dev = pos.device
+        owner = brick_of(pos, L, grid)
+        N = pos.shape[0]
+
+        def ghosts_of(r):
+            gid, img, own = select_local(pos, L, grid, r, halo)
+            gg, gi = gid[~own], img[~own]
+            order = torch.argsort(owner[gg] * N + gg)
+            return gid[own], img[own], gg[order], gi[order]
+
+        og, oi, gg, gi = ghosts_of(rank)
+        self.gid = torch.cat([og, gg])                       # local -> global id
+        self.img = torch.cat([oi, gi])                       # local position = global position + img
+        self.n_owned, self.n_ghost = int(og.numel()), int(gg.numel())
+        self.n_local = self.n_owned + self.n_ghost
+        own_g = gg.new_zeros(0)
+        self.recv_counts = [int((owner[gg] == q).sum()) for q in range(world)]
+        send, counts = [], []
+        for p in range(world):
+            if p == rank:
+                counts.append(0)
+                continue
+            _, _, gp, _ = ghosts_of(p)
+            mine = gp[owner[gp] == rank]                        # ascending global id (the peer's order)
+            send.append(torch.searchsorted(og, mine))
+            counts.append(int(mine.numel()))
+        self.send_idx = torch.cat(send) if send else og.new_zeros(0)
+        self.send_counts = counts
+        self.n_send = int(sum(counts))
+        del own_g
+
+
+class HaloExchange(torch.autograd.Function):
+    """y = x with its ghost rows (along `dim`) replaced by the owners' rows; x holds the local rows or only the owned
+    rows (then the ghost rows are appended).  Adjoint: the ghost rows' gradients go back to the owners (the reverse
+    all-to-all) and are added to the owned rows they came from."""
+
+    @staticmethod
+    def forward(ctx, x, plan, dim):
+        ctx.plan, ctx.dim, ctx.rows = plan, dim, x.shape[dim]
+        xs = x.movedim(dim, 0)
+        owned = xs[:plan.n_owned]
+        if plan.world == 1:
+            return owned.movedim(0, dim).contiguous()
+        send = owned[plan.send_idx].contiguous()
+        recv = xs.new_empty((plan.n_ghost,) + tuple(xs.shape[1:]))
+        dist.all_to_all_single(recv, send, plan.recv_counts, plan.send_counts, group=plan.group)
+        return torch.cat([owned, recv], 0).movedim(0, dim).contiguous()
+
+    @staticmethod
+    def backward(ctx, g):
+        plan, dim = ctx.plan, ctx.dim
+        gs = g.movedim(dim, 0)
+        go = gs[:plan.n_owned]
+        if plan.world > 1:
+            back = gs[plan.n_owned:].contiguous()
+            recv = gs.new_empty((plan.n_send,) + tuple(gs.shape[1:]))
+            dist.all_to_all_single(recv, back, plan.send_counts, plan.recv_counts, group=plan.group)
+            go = go.index_add(0, plan.send_idx, recv)
+        if ctx.rows > plan.n_owned:
+            go = torch.cat([go, gs.new_zeros((ctx.rows - plan.n_owned,) + tuple(gs.shape[1:]))], 0)
+        return go.movedim(0, dim).contiguous(), None, None
+
+
+def halo(x, plan, dim=0):
+    return HaloExchange.apply(x, plan, dim)
+
+
+def pass_exchange(plan, blocks_next, atom_dim):
+    """between(t, h, A_sets, eq) for the model's pass loop: the ghosts' features read by pass t + 1 at a neighbour
+    come from their owners.  atom_dim: (of h, of each A_sets tensor, of eq tensors)."""
+    dh, dA, de = atom_dim
+
+    def between(t, h, A_sets, eq):
+        nxt = blocks_next(t + 1)
+        h = halo(h, plan, dh)
+        if eq is not None:
+            eq = (halo(eq[0], plan, de), halo(eq[1], plan, de))
+        if nxt.get("directional") and not nxt.get("eq_in"):
+            A_sets = [[A[0], halo(A[1], plan, dA), halo(A[2], plan, dA), A[3]] for A in A_sets]
+        return h, A_sets, eq
+    return between
+
+
+def rank_energy(pos_owned, plan, local_model, coulomb=None):
+    """This rank's share of the total energy as a differentiable function of its owned atoms' positions.
+
+    local_model(pos_local) -> (e_at, h) over the local atoms (owned first; it applies the pass exchange itself).
+    coulomb (optional): dict with head(h) -> (chi, J); real_rows(pos_local, q_local) -> e_row; pme_slab(pos_owned,
+    q_owned) -> this rank's share of the reciprocal energy; gp, volume, charge (total charge Q).
     Sum over ranks = the system's energy."""
     from torch.distributed.nn import functional as dnn
-    pos_local = pos_global[gid] + img
+    no = plan.n_owned
+    pos_local = halo(pos_owned, plan, 0) + plan.img.to(pos_owned.dtype)
     e_at, h = local_model(pos_local)
-    w = owned.to(e_at.dtype)
-    e = (e_at * w).sum()
+    e = e_at[:no].sum()
     if coulomb is None:
         return e
     chi, J = coulomb["head"](h)
-    oi = torch.nonzero(owned)[:, 0]
-    chi_o, J_o = chi[oi], J[oi]
-    allr = (lambda x: dnn.all_reduce(x, group=group)) if world > 1 else (lambda x: x)
+    chi_o, J_o = chi[:no], J[:no]
+    allr = (lambda x: dnn.all_reduce(x, group=plan.group)) if plan.world > 1 else (lambda x: x)
     s1 = allr((chi_o / J_o).sum())
     s2 = allr((1.0 / J_o).sum())
     mu = (coulomb["charge"] + s1) / s2
     q_o = -(chi_o - mu) / J_o
-    # global charges: pad, all-gather, scatter by global id
-    n_g = coulomb["n_global"]
-    if world > 1:
-        pad = q_o.new_zeros(coulomb["max_owned"])
-        pad = torch.cat([q_o, pad[q_o.shape[0]:]])
-        parts = dnn.all_gather(pad, group=group)
-        flat = torch.cat(list(parts))
-    else:
-        flat = q_o
-    ids = coulomb["gid_owned_all"]
-    valid = ids >= 0
-    q_g = flat.new_zeros(n_g).index_put((ids[valid],), flat[valid])
-    q_loc = q_g[gid]
-    e_row = coulomb["real_rows"](pos_local, q_loc)
-    e_real = (e_row * w).sum()
-    if coulomb.get("pme_slab") is not None:          # this rank's k-space share of the mesh-distributed PME
-        e_recip_share = coulomb["pme_slab"](pos_global[gid[oi]], q_o)
-    else:                                            # full mesh on every rank, counted 1/world
-        e_recip_share = coulomb["pme"](pos_global, q_g) / world
+    q_loc = halo(q_o, plan, 0)
+    e_real = coulomb["real_rows"](pos_local, q_loc)[:no].sum()
+    e_recip_share = coulomb["pme_slab"](pos_local[:no], q_o)
     gp = coulomb["gp"]
     self_o = -(q_o * q_o).sum() / (math.sqrt(math.pi) * gp)
     qsum = allr(q_o.sum())
     bg = -0.5 * math.pi * gp ** 2 / coulomb["volume"] * qsum * qsum
-    e_es = KE * (e_real + e_recip_share + self_o + bg / world)
+    e_es = KE * (e_real + e_recip_share + self_o + bg / plan.world)
     return e + (chi_o * q_o + 0.5 * J_o * q_o * q_o).sum() + e_es
 
 
@@ -196,68 +286,17 @@ def _bspline_modulus2(n):
     return 1.0 / np.maximum(den, 1e-10)
 
 
-def owned_ids_all(gid, owned, world, group=None):
-    """Global ids of every rank's owned atoms in all-gather order, each rank padded to the largest count with -1."""
-    mine = gid[owned]
-    cnt = torch.tensor([mine.numel()], device=gid.device)
-    if world == 1:
-        return mine, int(mine.numel())
-    cnts = [torch.zeros_like(cnt) for _ in range(world)]
-    dist.all_gather(cnts, cnt, group=group)
-    mx = int(max(int(c) for c in cnts))
-    pad = torch.full((mx,), -1, dtype=mine.dtype, device=gid.device)
-    pad[:mine.numel()] = mine
-    parts = [torch.empty_like(pad) for _ in range(world)]
-    dist.all_gather(parts, pad, group=group)
-    return torch.cat(parts), mx
-
-
-# --------------------------------------------------------------------------------------------- GPU engine hooks
-class EngineParts:
-    """Callables of rank_energy backed by the CUDA engine (face_b200.ops)."""
-
-    def __init__(self, model, graph, pme_mesh, cell64):
-        from . import ops
-        self.ops = ops
-        self.model = model
-        self.g = graph
-        self.cell64 = cell64
-        self.P = None
-        self.geo = None
-        self.pme_mesh = pme_mesh
-
-    def local_model(self, pos_local):
-        e_at, h, P, gr, geo = self.ops.local_energies(self.model, self.g, pos_local)
-        self.P, self.gr, self.geo = P, gr, geo
-        return e_at, h
-
-    def head(self, h):
-        c = self.P["coulomb"]
-        import torch.nn.functional as F
-        chi, hard = self.ops._layer(c["h2"], F.silu(self.ops._layer(c["h0"], h))).unbind(-1)
-        return chi, F.softplus(hard) + 0.1
-
-    def real_rows(self, pos_local, q_local):
-        c = self.P["coulomb"]
-        return self.ops.CoulombReal.apply(self.geo["vec"], q_local.contiguous(), self.gr, c["gamma"], c["gp"])
-
-    def pme(self, pos_global, q_global):
-        c = self.P["coulomb"]
-        cell = np.asarray(self.cell64, np.float64)
-        return self.ops.PMERecip.apply(pos_global, q_global.contiguous(), np.linalg.inv(cell),
-                                       abs(float(np.linalg.det(cell))), c["gp"], tuple(self.pme_mesh))
-
-
+# --------------------------------------------------------------------------------------------- GPU engine
 class DistributedModel:
-    """Energy and forces of one periodic structure on `world` GPUs (this process = one rank)."""
+    """Energy and forces of one periodic structure on `world` GPUs (this process = one rank), with the per-pass halo
+    exchange.  `energy_forces(pos_owned)` takes this rank's owned positions (global ids `gid_owned`, in that order)
+    and returns (total energy, forces on the owned atoms)."""
 
-    def __init__(self, model, structure, rank, world, device, dtype=torch.float32, group=None, pme="replicated"):
-        """pme: "replicated" (the full mesh on every rank, counted 1/world) or "slab" (SlabPME: the mesh in x-slabs,
-        FFT transposed by an all-to-all; needs mesh dimensions 0 and 1 divisible by world)."""
-        from .neighbors import build_graph
-        if pme not in ("replicated", "slab"):
-            raise ValueError(f"pme={pme!r}")
-        self.pme_mode, self._slab = pme, None
+    def __init__(self, model, structure, rank, world, device, dtype=torch.float32, group=None, pme="slab"):
+        from . import ops
+        if pme != "slab":
+            raise ValueError("the halo decomposition distributes the PME mesh in slabs (pme='slab')")
+        self.ops, self.pme_mode = ops, pme
         self.model, self.rank, self.world, self.dev, self.dtype, self.group = model, rank, world, device, dtype, group
         cell = np.asarray(structure.cell, np.float64)
         if np.abs(cell - np.diag(np.diag(cell))).max() > 0:
@@ -265,53 +304,63 @@ class DistributedModel:
         self.L = np.diag(cell).copy()
         self.cell64 = cell
         self.grid = brick_grid(world)
-        self.halo = model.n_passes * model.rc
+        self.halo = model.rc
         for d in range(3):
             if self.grid[d] > 1 and self.L[d] / self.grid[d] + 2 * self.halo + model.rc >= self.L[d]:
                 raise ValueError(f"box too small for a {self.grid} decomposition with halo {self.halo} A")
-        self.numbers = np.asarray(structure.numbers, np.int64)
-        self.n_global = len(self.numbers)
         self.Q = float(getattr(structure, "charge", 0.0))
-        self.build_graph = build_graph
-        self.setup(torch.as_tensor(np.asarray(structure.positions), dtype=torch.float64, device=device))
-
-    def setup(self, pos64):
-        """(Re)build the decomposition and the local neighbour list for global positions pos64 (device)."""
-        gid, img, owned = select_local(pos64, self.L, self.grid, self.rank, self.halo)
-        self.gid, self.img, self.owned = gid, img, owned
-        loc = LocalSystem((pos64[gid] + img).cpu().numpy(), self.numbers[gid.cpu().numpy()], self.cell64)
-        self.graph = self.build_graph([loc], self.model.rc, device=self.dev, dtype=self.dtype)
-        self.img_t = img.to(self.dtype)
-        tm = self.model.terms["coulomb"] if "coulomb" in self.model.terms else None
-        self.parts = EngineParts(self.model, self.graph, None, self.cell64)
+        pos = torch.as_tensor(np.asarray(structure.positions), dtype=torch.float64, device=device)
+        self.plan = HaloPlan(pos, self.L, self.grid, rank, world, self.halo, group)
+        self.gid_owned = self.plan.gid[:self.plan.n_owned]
+        self.Z_local = torch.as_tensor(np.asarray(structure.numbers), dtype=torch.long, device=device)[self.plan.gid]
+        self.pos_owned = pos[self.gid_owned].to(dtype)          # this rank's coordinates (the only ones it keeps)
+        self.rebuild(pos[self.gid_owned])
+        self._slab = None
         self.coulomb = None
-        if tm is not None:
-            ids, mx = owned_ids_all(gid, owned, self.world, self.group)
+        if "coulomb" in model.terms:
+            tm = model.terms["coulomb"]
             mesh = tm.mesh or tuple(max(8, int(math.ceil(L / (tm.gp / 4.0)))) for L in self.L)
-            self.parts.pme_mesh = mesh
-            self.coulomb = {"head": self.parts.head, "real_rows": self.parts.real_rows, "pme": self.parts.pme,
-                            "gp": float(tm.gp), "volume": float(abs(np.linalg.det(self.cell64))), "charge": self.Q,
-                            "n_global": self.n_global, "gid_owned_all": ids, "max_owned": mx}
-            if self.pme_mode == "slab":
-                if self._slab is None:                  # the cell and mesh are fixed: Green's factors built once
-                    from . import ops
-                    cell64, mesh_t = self.cell64, tuple(mesh)
-                    self._slab = SlabPME(cell64, float(tm.gp), mesh_t, self.rank, self.world,
-                                         lambda p, q: ops.SpreadMesh.apply(p, q.contiguous(), cell64, mesh_t),
-                                         self.dtype, self.dev, self.group)
-                self.coulomb["pme_slab"] = self._slab
+            cell64, mesh_t = self.cell64, tuple(mesh)
+            self._slab = SlabPME(cell64, float(tm.gp), mesh_t, rank, world,
+                                 lambda p, q: ops.SpreadMesh.apply(p, q.contiguous(), cell64, mesh_t), dtype, device,
+                                 group)
+            self.coulomb = {"head": self.head, "real_rows": self.real_rows, "pme_slab": self._slab,
+                            "gp": float(tm.gp), "volume": float(abs(np.linalg.det(cell))), "charge": self.Q}
 
-    def energy_forces(self, pos_global):
-        """pos_global: (N,3) model-dtype device tensor of all atoms (same on every rank).  Returns (E_total, forces)
-        on every rank."""
-        pos = pos_global.detach().requires_grad_(True)
-        e = rank_energy(pos, self.gid, self.img_t, self.owned, self.parts.local_model, self.coulomb, self.world,
-                        self.group)
+    def rebuild(self, pos_owned64):
+        """Local neighbour list from this rank's owned float64 positions: ghost coordinates from their owners through
+        the halo, the list built on the device."""
+        from .neighbors import periodic_graph_device
+        with torch.no_grad():
+            loc = halo(pos_owned64.contiguous(), self.plan, 0) + self.plan.img
+        self.graph = periodic_graph_device(loc, self.Z_local, self.cell64, self.model.rc, self.dtype)
+
+    # engine callables of rank_energy
+    def local_model(self, pos_local):
+        P = self.ops.prepare(self.model, self.dtype, pos_local.device)
+        between = pass_exchange(self.plan, lambda t: P["blocks"][t], (0, 1, 1))
+        e_at, h, P, gr, geo = self.ops.local_energies(self.model, self.graph, pos_local, between=between)
+        self.P, self.gr, self.geo = P, gr, geo
+        return e_at, h
+
+    def head(self, h):
+        import torch.nn.functional as F
+        c = self.P["coulomb"]
+        chi, hard = self.ops._layer(c["h2"], F.silu(self.ops._layer(c["h0"], h))).unbind(-1)
+        return chi, F.softplus(hard) + 0.1
+
+    def real_rows(self, pos_local, q_local):
+        c = self.P["coulomb"]
+        return self.ops.CoulombReal.apply(self.geo["vec"], q_local.contiguous(), self.gr, c["gamma"], c["gp"])
+
+    def energy_forces(self, pos_owned=None):
+        """pos_owned: (n_owned, 3) model-dtype device tensor (default: the positions given at construction).
+        Returns (E_total on every rank, forces on the owned atoms)."""
+        pos = (self.pos_owned if pos_owned is None else pos_owned).detach().requires_grad_(True)
+        e = rank_energy(pos, self.plan, self.local_model, self.coulomb)
         (g,) = torch.autograd.grad(e, pos)
-        g = g.contiguous()
         et = e.detach().reshape(1).clone()
         if self.world > 1:
-            dist.all_reduce(g, group=self.group)
             dist.all_reduce(et, group=self.group)
         return et[0], -g
 
@@ -397,9 +446,9 @@ def bench_multi(a):
         model = B.make_model(spec, pme, dev, dtype)
         st = structs[0]
         natoms = len(st.numbers)
-        dm = DistributedModel(model, st, rank, world, dev, dtype, pme=getattr(a, "pme", "replicated"))
-        pos = torch.as_tensor(st.positions, dtype=dtype, device=dev)
-        n_local = int(dm.gid.numel())
+        dm = DistributedModel(model, st, rank, world, dev, dtype, pme="slab")
+        pos = dm.pos_owned                                   # this rank's owned coordinates only
+        n_local = dm.plan.n_local
         for _ in range(a.warmup):
             dm.energy_forces(pos)
         torch.cuda.synchronize()
@@ -433,25 +482,29 @@ def bench_multi(a):
         roof = perf.headline(rows, pk)
         if roof is not None:
             roof["kernel"] += ", rank 0 local system"
-        # e2e: positions from pinned host memory, decomposition + local neighbour list rebuilt, forces to the host
+        # e2e: each rank's owned coordinates from pinned host memory, ghost coordinates through the halo, the local
+        # neighbour list rebuilt on the device, forces on the owned atoms back to the host
         e2e = None
         if not a.no_e2e:
-            host = torch.as_tensor(st.positions, dtype=torch.float64).pin_memory()
+            host = torch.as_tensor(st.positions[dm.gid_owned.cpu().numpy()], dtype=torch.float64).pin_memory()
+            fh = torch.empty(host.shape, dtype=torch.float64).pin_memory()
             ke = max(1, a.steps // 2)
             torch.cuda.synchronize()
             dist.barrier()
             t0 = time.perf_counter()
             for _ in range(ke):
                 p64 = host.to(dev, non_blocking=True)
-                dm.setup(p64)
+                dm.rebuild(p64)
                 E, F = dm.energy_forces(p64.to(dtype))
-                Fh = F.double().cpu()
+                fh.copy_(F.double(), non_blocking=True)
+                torch.cuda.current_stream().synchronize()
             torch.cuda.synchronize()
             dist.barrier()
             dt = torch.tensor([(time.perf_counter() - t0) / ke], device=dev)
             dist.all_reduce(dt, op=dist.ReduceOp.MAX)
-            e2e = {"value": natoms / float(dt), "unit": B.UNIT, "h2d_bytes_per_step": natoms * 3 * 8,
-                   "d2h_bytes_per_step": natoms * 3 * 8, "ms_per_step": float(dt) * 1e3}
+            nb = int(host.numel()) * 8
+            e2e = {"value": natoms / float(dt), "unit": B.UNIT, "h2d_bytes_per_step": nb, "d2h_bytes_per_step": nb,
+                   "ms_per_step": float(dt) * 1e3, "note": "bytes per rank (its owned atoms); time max over ranks"}
         counts = torch.tensor([n_local], device=dev)
         allc = [torch.zeros_like(counts) for _ in range(world)]
         dist.all_gather(allc, counts)
@@ -463,7 +516,9 @@ def bench_multi(a):
                    "config": {"workload": f"cfg{a.config}: {natoms}-atom periodic system, spatial decomposition",
                               "atoms": natoms, "bricks": list(dm.grid), "halo_A": dm.halo,
                               "local_atoms_per_rank": [int(c) for c in allc],
-                              "l2": "inputs larger than L2", "parallelism": f"spatial {dm.grid} over NCCL", "pme": dm.pme_mode},
+                              "l2": "inputs larger than L2",
+                              "parallelism": f"spatial {dm.grid} over NCCL, rc-deep ghosts, per-pass halo exchange",
+                              "pme": "slab (mesh in x-slabs, all-to-all FFT transpose)"},
                    "e2e": e2e, "energy": float(E), "clocks": clk.summary(),
                    "roofline": roof,
                    "gpu_launches": int(launches)}

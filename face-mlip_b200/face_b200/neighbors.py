@@ -172,6 +172,28 @@ def _build_graph(structures, rc, device="cuda", dtype=torch.float32):
             "row_ptr": row_ptr, "ei": ei, "ej": ej, "S": S, "shift": shift, "rev": rev, "rc": float(rc)}
 
 
+def periodic_graph_device(pos64, Z, cell, rc, dtype=torch.float32):
+    """CSR graph of one periodic structure whose positions are already on the device (float64, (N, 3)); Z (N,) int64
+    on the device, cell (3, 3) host array.  Used by the spatial decomposition to rebuild a rank's local list from
+    halo-exchanged positions without a host round trip of the coordinates."""
+    dev = pos64.device
+    cell = np.asarray(cell, np.float64)
+    pos64 = pos64.contiguous()
+    N = pos64.shape[0]
+    rp, ei, ej, S, sh = _periodic_rows(pos64, cell, rc, dtype)
+    row_ptr = rp.to(torch.int32)
+    E = ei.numel()
+    rev = torch.empty(E, dtype=torch.int32, device=dev)
+    _lib.call("facek_nlist_reverse", _lib.ptr(row_ptr), _lib.ptr(ei), _lib.ptr(ej), _lib.ptr(S), N, E, _lib.ptr(rev),
+              _lib.stream())
+    return {"pos": pos64.to(dtype), "pos64": pos64, "meta": structure_meta([N], cell[None], dev), "Z": Z,
+            "batch": torch.zeros(N, dtype=torch.long, device=dev), "nstr": 1,
+            "natoms": torch.tensor([N], dtype=torch.long, device=dev),
+            "cell": torch.as_tensor(cell[None], dtype=dtype, device=dev), "cell64": cell[None], "pbc": [True],
+            "charge": torch.zeros(1, dtype=dtype, device=dev), "row_ptr": row_ptr, "ei": ei, "ej": ej, "S": S,
+            "shift": sh, "rev": rev, "rc": float(rc)}
+
+
 def to_padded(graph):
     """CSR graph -> the reference's padded-dense dict (face/datasets.py:74-97 layout)."""
     rp, ei, ej = graph["row_ptr"].long(), graph["ei"].long(), graph["ej"].long()

@@ -88,7 +88,7 @@ class Radial(torch.autograd.Function):
     @staticmethod
     def forward(ctx, vec, gr, blk):
         E = vec.shape[0]
-        B = blk["R"]                               # radial outputs: B, or B + 4C (CP), or 4C / 8C (non-factorised)
+        B = blk.get("R", blk["B"])                 # radial outputs: B, or B + 4C (CP), or 4C / 8C (non-factorised)
         phi = torch.empty(E, B, dtype=vec.dtype, device=vec.device)
         dphidr = torch.empty_like(phi)
         if blk.get("spline") is not None:
@@ -543,6 +543,54 @@ class SpreadMesh(torch.autograd.Function):
         return dpos, dq, None, None
 
 
+class LayerNormK(torch.autograd.Function):
+    """nn.LayerNorm over the last dimension with constant affine weights (face/model.py:140-141, :331) on the
+    library's warp-per-row kernel; the adjoint uses the per-row mean and 1/std saved by the forward."""
+
+    @staticmethod
+    def forward(ctx, x, w, b, eps):
+        x = x.contiguous()
+        N, W = x.shape
+        y = torch.empty_like(x)
+        mean = torch.empty(N, dtype=x.dtype, device=x.device)
+        rstd = torch.empty_like(mean)
+        _lib.call("facek_layer_norm_fwd", _tag(x), _p(x), _p(w), _p(b), float(eps), N, W, _p(y), _p(mean), _p(rstd),
+                  _lib.stream())
+        ctx.save_for_backward(x, w, mean, rstd)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        x, w, mean, rstd = ctx.saved_tensors
+        dx = torch.empty_like(x)
+        _lib.call("facek_layer_norm_bwd", _tag(x), _p(x), _p(w), _p(g.contiguous()), _p(mean), _p(rstd), x.shape[0],
+                  x.shape[1], _p(dx), _lib.stream())
+        return dx, None, None, None
+
+
+class SiLUK(torch.autograd.Function):
+    """x * sigmoid(x) on the library's elementwise kernel (the readout MLP's activations, face/model.py:73-77)."""
+
+    @staticmethod
+    def forward(ctx, x):
+        x = x.contiguous()
+        y = torch.empty_like(x)
+        _lib.call("facek_silu_fwd", _tag(x), _p(x), _p(y), x.numel(), _lib.stream())
+        ctx.save_for_backward(x)
+        return y
+
+    @staticmethod
+    def backward(ctx, g):
+        (x,) = ctx.saved_tensors
+        dx = torch.empty_like(x)
+        _lib.call("facek_silu_bwd", _tag(x), _p(x), _p(g.contiguous()), _p(dx), x.numel(), _lib.stream())
+        return dx
+
+
+def silu(x):
+    return SiLUK.apply(x) if x.is_cuda else F.silu(x)
+
+
 # ============================================================================================ channel GEMMs
 class Dense:
     """A constant (K, N) fp32 weight packed for the tensor-core GEMM (facek_gemm_tc): the split image of W for
@@ -663,6 +711,7 @@ def prepare(model, dtype, dev):
         pk = (lambda W, b=None: Dense(W, b) if tc and Dense.ok(*W.shape) else None)
         if blk.form != "moment":
             q["msg_w"], q["msg_b"] = _lin(model, blk.msg, dtype, dev)
+            q["msgD"] = pk(q["msg_w"].t(), q["msg_b"])
             # (B*K, C) factorised, (C, C) CP
             q["mixT"] = [(_lin(model, blk.mix[l], dtype, dev)[0]).t().contiguous() for l in range(4)]
             q["mixD"] = [pk(W) for W in q["mixT"]]
@@ -676,6 +725,19 @@ def prepare(model, dtype, dev):
             q["ln_w"], q["ln_b"] = d(blk.norm.w), d(blk.norm.b)
         q["out"] = [_lin(model, blk.out[i], dtype, dev) for i in (0, 2, 4)]
         q["outD"] = [pk(w.t(), b) for w, b in q["out"]]
+        # first readout layer split by input block [inv (9C) | h (C) | lognorms (4, zero here)]: two GEMMs into one
+        # output instead of a concatenated input (face/model.py:335)
+        w0, b0 = q["out"][0]
+        q["out0_inv"], q["out0_h"] = w0[:, :9 * C].t().contiguous(), w0[:, 9 * C:10 * C].t().contiguous()
+        q["out0_invD"], q["out0_hD"] = pk(q["out0_inv"], b0), pk(q["out0_h"])
+        # last readout layer (2C -> C + 1) zero-padded to a multiple of 4 output columns for the tensor-core GEMM
+        w4, b4 = q["out"][2]
+        n4 = (w4.shape[0] + 3) // 4 * 4
+        q["out4_pad"] = torch.zeros(w4.shape[1], n4, dtype=dtype, device=dev)
+        q["out4_pad"][:, :w4.shape[0]] = w4.t()
+        q["out4_b"] = torch.zeros(n4, dtype=dtype, device=dev)
+        q["out4_b"][:w4.shape[0]] = b4
+        q["out4D"] = pk(q["out4_pad"], q["out4_b"])
         if blk.eq_out:
             q["vpath"], q["mpath"] = d(blk.vpath), d(blk.mpath)
             q["gate"] = _lin(model, blk.gate, dtype, dev)
@@ -690,6 +752,7 @@ def prepare(model, dtype, dev):
             else:
                 q["pvtT"] = _lin(model, blk.pvt, dtype, dev)[0].t().contiguous()            # (cprev, nt*Kd)
                 q["pmtT"] = _lin(model, blk.pmt, dtype, dev)[0].t().contiguous()
+            q["pvtD"], q["pmtD"] = pk(q["pvtT"]), pk(q["pmtT"])
             q["y2w"] = torch.tensor(Y2W, dtype=dtype, device=dev)[:, None, None]
             # the y2 weights folded into per-component maps: (Md @ w) * y2w == Md @ (w * y2w), one batched matmul
             q["dir_y2"] = [q["y2w"] * q["dir"][i] for i in (1, 3)]                            # each (6, Kd, K)
@@ -804,13 +867,13 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
         A = channel_moments(q, gr, geo, h, A_sets, eq, phi)
         A = [BcastMul.apply(A[l], s[l]) for l in range(4)]
         return _invariants_readout(P, q, h, A_sets, A, N)
-    msgtab = F.linear(h, q["msg_w"], q["msg_b"])                                     # (N, K)
+    msgtab = linear(h, (q["msg_w"], q["msg_b"]), q["msgD"])                          # (N, K)
     Gt = None
     if q["directional"]:
         src1 = eq[0] if q["eq_in"] else torch.cat([A[1] for A in A_sets], 2)        # (3, N, cprev)
         src2 = eq[1] if q["eq_in"] else torch.cat([A[2] for A in A_sets], 2)        # (6, N, cprev)
-        Vb = src1 @ q["pvtT"]                                                        # (3, N, nt*Kd)
-        Mb = src2 @ q["pmtT"]                                                        # (6, N, nt*Kd)
+        Vb = mm(src1, q["pvtT"], q["pvtD"])                                           # (3, N, nt*Kd)
+        Mb = mm(src2, q["pmtT"], q["pmtD"])                                           # (6, N, nt*Kd)
         Vd, Md = Vb[..., :Kd], Mb[..., :Kd]
         w1, w2, w3, w4 = q["dir"]
         w2y, w4y = q["dir_y2"]
@@ -838,18 +901,27 @@ def _invariants_readout(P, q, h, A_sets, A, N):
     a_w = q["vpath"] if q["eq_out"] else None
     b_w = q["mpath"] if q["eq_out"] else None
     inv, V, Ms = NodeAlgebraEngine.apply(*ys, a_w, b_w, q["eq_out"], P["max_body"])
-    if q["norm"] == "layer":
+    if q["norm"] == "layer" and inv.shape[1] <= 768:
+        inv = LayerNormK.apply(inv, q["ln_w"], q["ln_b"], q["ln_eps"])
+    elif q["norm"] == "layer":                            # rows wider than the kernel's register tile (C > 85)
         inv = F.layer_norm(inv, (inv.shape[1],), q["ln_w"], q["ln_b"], q["ln_eps"])
     elif q["norm"] == "affine":
         inv = inv * q["ln_w"] + q["ln_b"]
-    z = torch.cat([inv, h, inv.new_zeros(N, 4)], 1)
-    o = linear(F.silu(linear(F.silu(linear(z, q["out"][0], q["outD"][0])), q["out"][1], q["outD"][1])),
-               q["out"][2], q["outD"][2])
+    # readout MLP on z = [inv | h | 0] (the reference's lognorm features are zero without momnorm, face/model.py:334)
+    if q["out0_invD"] is not None and q["out0_hD"] is not None:
+        o0 = TCMatmul.apply(inv, q["out0_invD"], h, q["out0_hD"])
+    else:
+        o0 = inv @ q["out0_inv"] + h @ q["out0_h"] + q["out"][0][1]
+    o1 = linear(silu(o0), q["out"][1], q["outD"][1])
+    if q["out4D"] is not None:
+        o = TCMatmul.apply(silu(o1), q["out4D"], None, None)             # (N, C + 1 padded to a multiple of 4)
+    else:
+        o = linear(silu(o1), q["out"][2], None)
     eq_new = None
     if q["eq_out"]:
         gv, gm = linear(inv, q["gate"], q["gateD"]).chunk(2, dim=-1)
         eq_new = (BcastMul.apply(V, gv), BcastMul.apply(Ms, gm))
-    return o[:, 0], h + o[:, 1:], A, eq_new
+    return o[:, 0], h + o[:, 1:h.shape[1] + 1], A, eq_new
 
 
 def seg_sum(x, batch, nstr):
@@ -923,9 +995,13 @@ def coulomb_term(P, gr, geo, h, pos):
     return chi * q + 0.5 * J * q * q + per_atom(e_es / natoms.to(q.dtype), batch, nstr), q
 
 
-def local_energies(model, gr, pos):
+def local_energies(model, gr, pos, between=None):
     """Per-atom model energies (without physics terms) and final features h for positions `pos` (any
-    differentiable tensor) on graph `gr` (face/model.py:665-686)."""
+    differentiable tensor) on graph `gr` (face/model.py:665-686).
+
+    between(t, h, A_sets, eq) -> (h, A_sets, eq), when given, runs after every pass but the last: the spatial
+    decomposition replaces its ghost atoms' features there with their owners' (a halo exchange).  Layouts: h (N, C),
+    each A_sets[k][l] (k_l, N, C), eq = (V (3, N, C), Ms (6, N, C)) or None."""
     dtype = model.embed.weight.dtype
     P = prepare(model, dtype, pos.device)
     P["max_body"] = model.max_body
@@ -937,10 +1013,13 @@ def local_energies(model, gr, pos):
     h = P["embed"][zidx]
     e_at = P["E0"][zidx]
     A_sets, eq = [], None
-    for t in range(len(P["blocks"])):
+    n = len(P["blocks"])
+    for t in range(n):
         e, h, A, eq = block_forward(P, t, gr, geo, h, A_sets, eq)
         A_sets.append(A)
         e_at = e_at + P["scale"] * e
+        if between is not None and t + 1 < n:
+            h, A_sets, eq = between(t, h, A_sets, eq)
     return e_at, h, P, gr, geo
 
 

@@ -267,6 +267,19 @@ int facek_cp_density_bwd(int dtype, const void* Y, const void* R, int64_t ldr, i
                          void* dR, void* dm, void* dY, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------
+ * Readout elementwise kernels (face/model.py:331-339): LayerNorm over rows of W <= 768 features with constant affine
+ * weights (nn.LayerNorm: biased variance, y = (x - mean) / sqrt(var + eps) * w + b); the forward stores mean and
+ * 1/std per row for the adjoint dx = rstd (g w - mean(g w) - xhat mean(g w xhat)).  SiLU y = x sigmoid(x) and its
+ * adjoint.
+ */
+int facek_layer_norm_fwd(int dtype, const void* x, const void* w, const void* b, double eps, int64_t N, int32_t W,
+                         void* y, void* mean, void* rstd, void* stream);
+int facek_layer_norm_bwd(int dtype, const void* x, const void* w, const void* g, const void* mean, const void* rstd,
+                         int64_t N, int32_t W, void* dx, void* stream);
+int facek_silu_fwd(int dtype, const void* x, void* y, int64_t n, void* stream);
+int facek_silu_bwd(int dtype, const void* x, const void* g, void* dx, int64_t n, void* stream);
+
+/* ---------------------------------------------------------------------------------------------------
  * Pair physics terms, per CSR row over a symmetric neighbour list (vec from facek_edge_vec of that list).
  * ZBL (face/model.py:538-554, the "zbl" term): e_row[i] = 1/2 sum_{e in row i} KE Zi Zj / r phi(r/a) s(r),
  *   a = 0.46850 / (Zi^0.23 + Zj^0.23), phi the universal 4-exponential screening, s the quintic switch from 1 at

@@ -70,12 +70,18 @@ def neighbor_list_ijS(positions, cell, pbc, rc, chunk=256):
         rng = [np.arange(-m[d], m[d] + 1) for d in range(3)]
         imgs = np.stack(np.meshgrid(*rng, indexing="ij"), -1).reshape(-1, 3)
         isv = imgs.astype(np.float64) @ cell                     # candidate filter only
+        # candidates: every (i, j, image) whose wrapped-frame distance is below rc + 1e-6, from a k-d tree over all
+        # images of the wrapped atoms (a superset of the pairs the exact test below keeps)
+        from scipy.spatial import cKDTree
+        pts = (pw[None, :, :] + isv[:, None, :]).reshape(-1, 3)  # index = image * n + j
+        tree = cKDTree(pts)
         I, J, S = [], [], []
-        for a in range(0, n, chunk):
-            d = pw[None, :, None, :] - pw[a:a + chunk, None, None, :] + isv[None, None]
-            r2 = (d * d).sum(-1)
-            ii, jj, kk = np.nonzero(r2 < (rc + 1e-6) ** 2)
-            ii = ii + a
+        for a in range(0, n, 4096):
+            hits = tree.query_ball_point(pw[a:a + 4096], rc + 1e-6)
+            cnt = np.fromiter((len(h) for h in hits), np.int64, len(hits))
+            flat = np.fromiter((x for h in hits for x in h), np.int64, int(cnt.sum()))
+            ii = np.repeat(np.arange(a, a + len(hits)), cnt)
+            kk, jj = flat // n, flat % n
             I.append(ii); J.append(jj)
             # shift in the original (unwrapped) frame: pw_j - pw_i + s.cell = pos_j - pos_i + (s - w_j + w_i).cell
             S.append(imgs[kk] - w[jj].astype(np.int64) + w[ii].astype(np.int64))

@@ -8,8 +8,9 @@ import numpy as np
 
 GOLDEN = os.path.join(os.path.dirname(os.path.abspath(__file__)), "golden")
 SMALL_CASES = ["cfg1", "cfg1_spline", "cfg2", "cfg3_small", "cfg4_small", "cfg5_small"]
-# the benchmark configurations at full size (cfg3: 15,590 atoms; cfg4: 32,768 atoms) and a 37,044-atom cfg5 sub-box
-FULL_CASES = ["cfg3", "cfg4", "cfg5_37k"]
+# cfg3 at full size (15,590 atoms), a 16,384-atom cfg4 box (the full 32,768-atom box does not fit the reference's
+# evaluation on the host that made the fixtures) and a 37,044-atom cfg5 sub-box
+FULL_CASES = ["cfg3", "cfg4_16k", "cfg5_37k"]
 # physics terms: ZBL and dispersion (the latter needs the 10 A long-range list, rc_long below)
 TERM_CASES = ["zbl_mol", "disp_mol", "disp_nacl"]
 RC_LONG = 10.0

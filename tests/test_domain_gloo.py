@@ -1,8 +1,10 @@
-"""Spatial decomposition and its collective assembly (face_b200/domain.py) on two CPU ranks (gloo).
+"""Spatial decomposition with the per-pass halo exchange (face_b200/domain.py) on two CPU ranks (gloo).
 
-The local model is the CPU oracle, so this checks the multi-GPU logic without a GPU: brick selection, ghost images,
-owned-atom energies, the all-reduced neutrality sums, the all-gathered global charges feeding real space and PME,
-and the all-reduced force gradient -- against the oracle evaluated on the whole periodic system in one process.
+The local model is the CPU oracle, so this checks the multi-GPU logic without a GPU: brick selection, rc-deep ghost
+images, the halo plan (owners, send and receive lists), the differentiable halo exchange of positions, of the pass-1
+features and of the charges (forward rows from the owners, gradients back to them), the all-reduced neutrality sums
+and the slab-distributed PME -- against the oracle evaluated on the whole periodic system in one process.  No rank
+holds the global positions after setup and no N x 3 gradient is all-reduced.
 """
 import datetime
 import math
@@ -41,12 +43,14 @@ def _state():
     return {k: v.double() if v.is_floating_point() else v for k, v in m.seed_(3).state_dict().items()}
 
 
-def _oracle_parts(P, cfg, g_local, cell):
+def _oracle_parts(P, cfg, g_local, plan):
+    from face_b200 import domain
     gamma = 1.0
     gp = PME["gp"]
+    between = domain.pass_exchange(plan, lambda t: {"directional": True, "eq_in": cfg["eqmsg"]}, (0, 0, 0))
 
     def local_model(pos_local):
-        return face_ref.atom_energies(P, cfg, g_local, pos_local, torch.float64)
+        return face_ref.atom_energies(P, cfg, g_local, pos_local, torch.float64, between=between)
 
     def head(h):
         chi, hard = P.lin("terms.coulomb.head.2", torch.nn.functional.silu(P.lin("terms.coulomb.head.0", h))).unbind(-1)
@@ -62,10 +66,7 @@ def _oracle_parts(P, cfg, g_local, cell):
         K = torch.where(mask, (torch.erf(r / gamma) - torch.erf(r / gp)) / r, torch.zeros_like(r))
         return 0.5 * q_local * (q_local[nbr] * K).sum(1)
 
-    def pme(pos_global, q_global):
-        return face_ref.pme_recip_energy(q_global, pos_global, torch.as_tensor(cell), gp, PME["mesh"])
-
-    return local_model, head, real_rows, pme
+    return local_model, head, real_rows
 
 
 def _oracle_spread(cell, mesh):
@@ -85,7 +86,7 @@ def _oracle_spread(cell, mesh):
     return spread
 
 
-def _worker(rank, world, port, out, mode="replicated"):
+def _worker(rank, world, port, out):
     os.environ["MASTER_ADDR"] = "127.0.0.1"
     os.environ["MASTER_PORT"] = str(port)
     # a short timeout so that a rank left waiting for a failed peer ends with an error instead of hanging
@@ -98,25 +99,39 @@ def _worker(rank, world, port, out, mode="replicated"):
         pos_g = torch.as_tensor(st.positions, dtype=torch.float64)
         L = np.diag(st.cell)
         grid = domain.brick_grid(world)
-        gid, img, owned = domain.select_local(pos_g, L, grid, rank, cfg["n_passes"] * cfg["rc"])
-        loc = domain.LocalSystem((pos_g[gid] + img).numpy(), st.numbers[gid.numpy()], st.cell)
-        g_local = nlist.padded_graph([loc], cfg["rc"])
-        local_model, head, real_rows, pme = _oracle_parts(P, cfg, g_local, st.cell)
-        ids, mx = domain.owned_ids_all(gid, owned, world)
-        coul = {"head": head, "real_rows": real_rows, "pme": pme, "gp": PME["gp"],
-                "volume": float(abs(np.linalg.det(st.cell))), "charge": 0.0, "n_global": len(st.numbers),
-                "gid_owned_all": ids, "max_owned": mx}
-        if mode == "slab":
-            coul["pme_slab"] = domain.SlabPME(st.cell, PME["gp"], PME["mesh"], rank, world,
-                                              _oracle_spread(st.cell, PME["mesh"]), torch.float64, "cpu")
-        pos = pos_g.clone().requires_grad_(True)
-        e = domain.rank_energy(pos, gid, img, owned, local_model, coul, world)
+        plan = domain.HaloPlan(pos_g, L, grid, rank, world, cfg["rc"])        # rc-deep ghosts
+        pos_local = (pos_g[plan.gid] + plan.img).numpy()
+        g_local = nlist.padded_graph([domain.LocalSystem(pos_local, st.numbers[plan.gid.numpy()], st.cell)], cfg["rc"])
+        local_model, head, real_rows = _oracle_parts(P, cfg, g_local, plan)
+        coul = {"head": head, "real_rows": real_rows, "gp": PME["gp"], "volume": float(abs(np.linalg.det(st.cell))),
+                "charge": 0.0,
+                "pme_slab": domain.SlabPME(st.cell, PME["gp"], PME["mesh"], rank, world,
+                                           _oracle_spread(st.cell, PME["mesh"]), torch.float64, "cpu")}
+        gid_owned = plan.gid[:plan.n_owned]
+        pos = pos_g[gid_owned].clone().requires_grad_(True)                 # this rank's coordinates only
+        e = domain.rank_energy(pos, plan, local_model, coul)
         (g,) = torch.autograd.grad(e, pos)
         et = e.detach().reshape(1).clone()
-        dist.all_reduce(g)
         dist.all_reduce(et)
+        # collect the owned forces on rank 0 for the comparison (test harness only)
+        n = torch.tensor([plan.n_owned])
+        sizes = [torch.zeros_like(n) for _ in range(world)]
+        dist.all_gather(sizes, n)
+        mx = int(max(int(x) for x in sizes))
+        pad_f = torch.zeros(mx, 3, dtype=torch.float64)
+        pad_f[:plan.n_owned] = -g
+        pad_i = torch.full((mx,), -1, dtype=torch.long)
+        pad_i[:plan.n_owned] = gid_owned
+        fs = [torch.zeros_like(pad_f) for _ in range(world)]
+        ids = [torch.zeros_like(pad_i) for _ in range(world)]
+        dist.all_gather(fs, pad_f)
+        dist.all_gather(ids, pad_i)
         if rank == 0:
-            out.put((float(et[0]), (-g).numpy(), int(owned.sum()), int(gid.numel())))
+            F = np.zeros((len(st.numbers), 3))
+            for f, i in zip(fs, ids):
+                k = i >= 0
+                F[i[k].numpy()] = f[k].numpy()
+            out.put((float(et[0]), F, plan.n_owned, plan.n_local, plan.n_send, sum(plan.recv_counts)))
             out.close()
             out.join_thread()                          # the result is in the pipe before this process ends
         dist.barrier()                                 # both ranks are out of their last collective
@@ -136,10 +151,7 @@ def _free_port():
     return p
 
 
-@pytest.mark.parametrize("mode", ["replicated", "slab"])
-def test_two_rank_decomposition_matches_single_system(mode):
-    """mode "replicated": the PME mesh on every rank; "slab": the mesh in x-slabs with the FFT transposed by an
-    all-to-all (SlabPME)."""
+def test_two_rank_halo_decomposition_matches_single_system():
     st = _system()
     cfg = dict(SPEC)
     g = nlist.padded_graph([st], cfg["rc"])
@@ -147,14 +159,14 @@ def test_two_rank_decomposition_matches_single_system(mode):
     ctx = mp.get_context("spawn")
     q = ctx.Queue()
     port = _free_port()
-    procs = [ctx.Process(target=_worker, args=(r, 2, port, q, mode)) for r in range(2)]
+    procs = [ctx.Process(target=_worker, args=(r, 2, port, q)) for r in range(2)]
     for p in procs:
         p.start()
-    E, F, n_owned, n_local = q.get(timeout=600)
+    E, F, n_owned, n_local, n_send, n_recv = q.get(timeout=600)
     for p in procs:
         p.join(timeout=120)
         assert p.exitcode == 0
-    assert n_local > n_owned                       # ghosts present
+    assert n_local > n_owned and n_send > 0 and n_recv == n_local - n_owned     # ghosts exchanged
     assert abs(E - float(ref["energy"][0])) <= 1e-10 * abs(float(ref["energy"][0]))
     assert np.abs(F - ref["forces"].numpy()).max() <= 1e-9
 

@@ -44,7 +44,9 @@ def test_evaluation_issues_no_host_sync(case):
         o = m(dict(g, pos=g["pos"].clone()))
     finally:
         torch.cuda.set_sync_debug_mode("default")
-    assert torch.equal(o["energy"], ref["energy"]) and torch.equal(o["forces"], ref["forces"])
+    # same result (not bit for bit: the PME charge spreading adds with atomics, in no fixed order)
+    assert float((o["energy"] - ref["energy"]).abs().max()) <= 1e-6 * float(ref["energy"].abs().max())
+    assert float((o["forces"] - ref["forces"]).abs().max()) <= 1e-5
 
 
 @pytest.mark.parametrize("dtype", [torch.float64, torch.float32])
@@ -61,7 +63,7 @@ def test_calculator_skin_reuse_matches_fresh_lists(dtype):
     rng = np.random.default_rng(0)
     pos = st.positions.copy()
     for step in range(8):
-        pos = pos + rng.normal(0, 0.06, pos.shape)            # random walk: the 0.5 A trigger is crossed midway
+        pos = pos + rng.normal(0, 0.12, pos.shape)            # random walk: the 0.5 A trigger is crossed midway
         at = systems.Structure(pos.copy(), st.numbers, st.cell, True)
         fresh.calculate(at)
         reuse.calculate(at)
