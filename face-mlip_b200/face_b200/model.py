@@ -1,9 +1,10 @@
 """FACE energy+force engine for B200 (sm_100a).
 
 Drop-in for face-mlip's `face.model.FACE` on the inference hot path `FACE.forward(g, forces=True)`
-(face-mlip `face/model.py:558-695`): same constructor, same `state_dict` keys (checkpoints load unchanged),
-same `set_*` / `fuse()` / `compile_radial()` switches, same graph-dict input and output dict
-({"energy", "atom_energy", "forces"}).
+(face-mlip `face/model.py:558-695`): same constructor, same `state_dict` keys (checkpoints of the factorised,
+CP and non-factorised forms load unchanged), same `set_*` / `fuse()` / `compile_radial()` switches (the ones the
+engine does not implement raise), same graph-dict input and output dict ({"energy", "atom_energy", "forces"}),
+physics terms coulomb, zbl and disp.
 
 The edge-level work (geometry, radial basis x radial MLP, the factorised Cartesian density, directional
 messages, transport sums, their analytic backward and the force gather) runs in the hand-written CUDA

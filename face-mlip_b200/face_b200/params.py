@@ -1,5 +1,5 @@
 """Parameter layout of face-mlip's FACE model (same state_dict keys and shapes as the reference, so its
-checkpoints load unchanged) and deterministic seeded weights.
+checkpoints of the three block forms load unchanged) and deterministic seeded weights.
 
 Key layout follows face-mlip `face/model.py`:
   embed (Embedding n_el x C) :570 ; buffers zmap/E0/scale/avg_nb/basis.freq :564-578
