@@ -9,7 +9,7 @@ import os
 import torch
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libfacek.so")
+LIB_PATH = os.environ.get("FACEK_LIB") or os.path.join(_HERE, "libfacek.so")    # FACEK_LIB: another build
 
 F32, F64 = 0, 1
 P = ctypes.c_void_p

@@ -20,6 +20,8 @@ ghost rows from their owners forward, and of the ghost gradients back to the own
     (SlabPME: each rank spreads its owned charges, reduce-scatter into x-slabs, 2-D FFT, all-to-all transpose, 1-D
     FFT);
   * energy: one all-reduced scalar.
+Ghost rows keep only their edges to owned atoms (the reverse edges the adjoint gathers need): their outputs are
+overwritten by the halo or dropped, so ghost-ghost edges would be wasted work.
 Every rank runs the same collectives in the same order, forward and backward.
 """
 import json
@@ -330,10 +332,14 @@ class DistributedModel:
     def rebuild(self, pos_owned64):
         """Local neighbour list from this rank's owned float64 positions: ghost coordinates from their owners through
         the halo, the list built on the device."""
-        from .neighbors import periodic_graph_device
+        from .neighbors import keep_edges, periodic_graph_device
         with torch.no_grad():
             loc = halo(pos_owned64.contiguous(), self.plan, 0) + self.plan.img
-        self.graph = periodic_graph_device(loc, self.Z_local, self.cell64, self.model.rc, self.dtype)
+        g = periodic_graph_device(loc, self.Z_local, self.cell64, self.model.rc, self.dtype)
+        # ghost-ghost edges only feed ghost rows, whose outputs the halo overwrites (pass 1) or the energy drops
+        # (last pass): keep the edges that touch an owned atom (a symmetric condition, so reverse edges stay)
+        no = self.plan.n_owned
+        self.graph = keep_edges(g, (g["ei"] < no) | (g["ej"] < no)) if self.world > 1 else g
 
     # engine callables of rank_energy
     def local_model(self, pos_local):

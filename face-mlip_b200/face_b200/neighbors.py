@@ -194,6 +194,20 @@ def periodic_graph_device(pos64, Z, cell, rc, dtype=torch.float32):
             "shift": sh, "rev": rev, "rc": float(rc)}
 
 
+def keep_edges(g, keep):
+    """The graph restricted to the edges where `keep` (E,) is true; `keep` must be symmetric (an edge and its reverse
+    kept together), so that rows stay in canonical order and every kept edge keeps its reverse."""
+    idx = torch.nonzero(keep)[:, 0]
+    N = g["row_ptr"].numel() - 1
+    ei, ej, S, sh = g["ei"][idx].contiguous(), g["ej"][idx].contiguous(), g["S"][idx].contiguous(), g["shift"][idx]
+    row_ptr = _cumsum0(torch.bincount(ei.long(), minlength=N)).to(torch.int32)
+    E = ei.numel()
+    rev = torch.empty(E, dtype=torch.int32, device=ei.device)
+    _lib.call("facek_nlist_reverse", _lib.ptr(row_ptr), _lib.ptr(ei), _lib.ptr(ej), _lib.ptr(S), N, E, _lib.ptr(rev),
+              _lib.stream())
+    return dict(g, row_ptr=row_ptr, ei=ei, ej=ej, S=S, shift=sh.contiguous(), rev=rev)
+
+
 def to_padded(graph):
     """CSR graph -> the reference's padded-dense dict (face/datasets.py:74-97 layout)."""
     rp, ei, ej = graph["row_ptr"].long(), graph["ei"].long(), graph["ej"].long()

@@ -79,6 +79,7 @@ def collect(E, N, B, K, esz, steps, root, traffic=None):
         t_bound = max(b_tot / (pk["hbm_gbs"] * 1e9), 0.0 if key == "gemm" else f_tot / (pk["fp32_tflops"] * 1e12))
         row = {"kernel": KERNEL_NAMES[key], "launches_per_step": launches / steps,
                "ms_per_step": t_tot * 1e3 / steps, "launch_ms": statistics.mean(ts) * 1e3,
+               "launch_ms_first_step": [round(t * 1e3, 3) for t in ts[:launches // steps]],
                "bytes_per_launch": b_tot / launches, "flops_per_launch": f_tot / launches,
                "hbm": {"achieved": gbs, "peak": pk["hbm_gbs"], "unit": "GB/s", "frac": gbs / pk["hbm_gbs"]},
                "fp32": None if key == "gemm" else

@@ -102,6 +102,9 @@ def _worker(rank, world, port, out):
         plan = domain.HaloPlan(pos_g, L, grid, rank, world, cfg["rc"])        # rc-deep ghosts
         pos_local = (pos_g[plan.gid] + plan.img).numpy()
         g_local = nlist.padded_graph([domain.LocalSystem(pos_local, st.numbers[plan.gid.numpy()], st.cell)], cfg["rc"])
+        # as on the GPU: ghost rows keep only their edges to owned atoms
+        no = plan.n_owned
+        g_local["mask"] &= (np.arange(plan.n_local)[:, None] < no) | (g_local["nbr"] < no)
         local_model, head, real_rows = _oracle_parts(P, cfg, g_local, plan)
         coul = {"head": head, "real_rows": real_rows, "gp": PME["gp"], "volume": float(abs(np.linalg.det(st.cell))),
                 "charge": 0.0,
