@@ -330,6 +330,284 @@ int density_tc_xm_fwd(const float* phi, const float* msg, const float* Y, float*
   return launch_status("facek_density_tc_xm_fwd");
 }
 
+// ===================================================================================================================
+// Density adjoint on the tensor cores (fp32, B = 16, K = 32, CSR rows, component-major G planes).  Per atom i and a
+// chunk of up to 128 of its edges (the MMA's M), two small GEMMs against the atom's G (20 x 16 x 32):
+//   T[e, (x, b)] = sum_k msg[e, k] G[x, b, k]        N = 320, K = 32     (B operand: G rows (x, b), K-major)
+//   U[e, (x, k)] = sum_b phi[e, b] G[x, b, k]        N = 640, K = 16     (B operand: G transposed, rows (x, k))
+// and a per-edge epilogue on the CUDA cores (one thread per TMEM lane = edge row):
+//   dY[e, x] = sum_b phi[e, b] T[e, (x, b)],  dphi[e, b] = sum_x Y[e, x] T[e, (x, b)],
+//   dmsg[e, k] = sum_x Y[e, x] U[e, (x, k)]
+// -- 1.3 k FMAs per edge instead of the 20 k of the lane-per-edge contraction.  The message part of dY is added
+// afterwards by the message kernel (edge_msg_dy).
+// fp32 accuracy by the 3-term tf32 split of both operands (tc.cuh); an accumulator sums at most 12 MMAs.
+// Status: parity-green, opt-in (facek_density_msg_tc_xm_bwd); slower than the lane-per-edge kernel on the cfg5 alloy
+// (105-111 vs 65-70 ms per launch).  Cycles per atom measured with clock64 on the scale-24 alloy: operand staging
+// 12.3 k (59%: G's 40 KB written as hi and lo in both orientations by one CTA per SM, nothing overlapping it), MMA
+// phase 1 2.7 k, epilogue 1 2.0 k, MMA phase 2 1.8 k, epilogue 2 1.5 k -- the 48 MMAs cost ~90 cycles each; hiding
+// the staging needs a second 160 KB G buffer, which does not fit.
+// Operands: K-major, no swizzle (kmajor_off).  Tensor memory: 512 columns; phase 1 holds T (columns 0..319) and U for
+// x < 5 (320..479), phase 2 U for x >= 5 (0..479).  One CTA per SM (208 KB of shared memory): warps 0-3 stage the
+// operands and run the epilogue, thread 128 issues the MMAs.  Every wait is bounded.
+namespace {
+constexpr int kAX = 20, kAB = 16, kAK = 32;
+constexpr int kARows = 128;                                  // edges per chunk (MMA M)
+constexpr int kANT = kAX * kAB;                              // 320 T columns
+constexpr int kANU = kAX * kAK;                              // 640 U columns
+constexpr uint32_t kAPlaneB = kANT * kAK * 4;                // 40 KB, one (hi or lo) plane of either B operand
+constexpr uint32_t kAPlaneM = kARows * kAK * 4;              // 16 KB, msg plane
+constexpr uint32_t kAPlaneP = kARows * kAB * 4;              // 8 KB, phi plane
+constexpr uint32_t oBTh = 0, oBTl = oBTh + kAPlaneB, oBUh = oBTl + kAPlaneB, oBUl = oBUh + kAPlaneB;
+constexpr uint32_t oAMh = oBUl + kAPlaneB, oAMl = oAMh + kAPlaneM, oAPh = oAMl + kAPlaneM, oAPl = oAPh + kAPlaneP;
+constexpr uint32_t oABar = oAPl + kAPlaneP;
+constexpr uint32_t kASmem = oABar + 64;
+constexpr int kAThreads = 160;
+constexpr int kAN = 160;                                     // N of one MMA (320 = 2 x 160, 640 = 4 x 160)
+static_assert(kAX * 128 % (kAThreads * 8) == 0, "G staging assumes an even split into batches of 8 per thread");
+
+struct GPlanes {                                             // component-major G: rank planes, x stride, atom stride
+  const float* base[4];
+  int64_t sX, sN;
+  __device__ __forceinline__ const float* at(int64_t i, int x) const {
+    const float* b = x < 1 ? base[0] : (x < 4 ? base[1] : (x < 10 ? base[2] : base[3]));
+    const int o = x < 1 ? 0 : (x < 4 ? 1 : (x < 10 ? 4 : 10));
+    return b + (int64_t)(x - o) * sX + i * sN;
+  }
+};
+
+// G of atom i -> both B operands (hi, lo): BT rows (x, b) x K = k, BU rows (x, k) x K = b
+__device__ __forceinline__ void stage_g(unsigned char* sm, const GPlanes& G, int64_t i, int tid) {
+  // all of this thread's 16 loads in flight first (kAX * 128 = 2560 float4 over 160 threads), then the stores
+  constexpr int kPer = kAX * 128 / kAThreads, kBatch = 8;
+#pragma unroll 1
+  for (int r0 = 0; r0 < kPer; r0 += kBatch) {
+  float4 buf[kBatch];
+#pragma unroll
+  for (int r = 0; r < kBatch; r++) {
+    const int q = tid + (r0 + r) * kAThreads;
+    buf[r] = __ldg(reinterpret_cast<const float4*>(G.at(i, q >> 7)) + (q & 127));
+  }
+#pragma unroll
+  for (int r = 0; r < kBatch; r++) {
+    const int q = tid + (r0 + r) * kAThreads;
+    const int x = q >> 7, f = q & 127, b = f >> 3, k0 = (f & 7) * 4;
+    const float4 v = buf[r];
+    store_split4(sm + oBTh, sm + oBTl, kmajor_off(x * kAB + b, k0, kANT), v.x, v.y, v.z, v.w);
+    const float vv[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+    for (int j = 0; j < 4; j++) {
+      const float h = to_tf32(vv[j]);
+      const uint32_t off = kmajor_off(x * kAK + k0 + j, b, kANU);
+      *reinterpret_cast<float*>(sm + oBUh + off) = h;
+      *reinterpret_cast<float*>(sm + oBUl + off) = to_tf32(vv[j] - h);
+    }
+  }
+  }
+}
+
+// D[d_col .. +160) (+)= A . B[rows n0 .. n0+160)^T over K = 8 * nks, 3-term split; A planes of kARows rows
+__device__ __forceinline__ void mma_split(uint32_t d, uint32_t a_hi, uint32_t a_lo, uint32_t b_hi, uint32_t b_lo,
+                                          uint32_t b_rows, uint32_t n0, int nks) {
+  const uint32_t idesc = idesc_tf32(kARows, kAN);
+  for (int s = 0; s < nks; s++) {
+    const uint64_t ah = desc_kmajor(a_hi + s * 2 * kARows * 16, kARows * 16, 128);
+    const uint64_t al = desc_kmajor(a_lo + s * 2 * kARows * 16, kARows * 16, 128);
+    const uint32_t boff = s * 2 * b_rows * 16 + (n0 / 8) * 128;
+    const uint64_t bh = desc_kmajor(b_hi + boff, b_rows * 16, 128);
+    const uint64_t bl = desc_kmajor(b_lo + boff, b_rows * 16, 128);
+    mma_tf32(d, al, bh, idesc, s > 0 ? 1u : 0u);
+    mma_tf32(d, ah, bl, idesc, 1u);
+    mma_tf32(d, ah, bh, idesc, 1u);
+  }
+}
+
+// the 16 fp32 columns [c, c + 16) of this warp's 32 TMEM lanes, twice (two loads in flight)
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, float* v) {
+  tmem_ld16(taddr, v);
+  tmem_ld16(taddr + 16, v + 16);
+  tmem_wait_ld();
+}
+
+__global__ void __launch_bounds__(kAThreads, 1)
+    dens_bwd_tc_k(const float* __restrict__ phi, const float* __restrict__ msg, const float* __restrict__ Y,
+                  GPlanes G, float* __restrict__ dphi, float* __restrict__ dmsg, float* __restrict__ dY, int64_t N,
+                  const int32_t* __restrict__ row_ptr) {
+  extern __shared__ __align__(1024) unsigned char sm[];
+  uint64_t* mbar = reinterpret_cast<uint64_t*>(sm + oABar);
+  uint32_t* slot = reinterpret_cast<uint32_t*>(sm + oABar + 8);
+  int* abort_ = reinterpret_cast<int*>(sm + oABar + 16);
+  const int tid = threadIdx.x, warp = tid >> 5, lane = tid & 31;
+  if (tid == 0) {
+    *abort_ = 0;
+    mbar_init(mbar, 1);
+    fence_mbar_init();
+  }
+  if (warp == 0) {
+    tmem_alloc(slot, 512);
+    tmem_relinquish();
+  }
+  fence_before_sync();
+  __syncthreads();
+  fence_after_sync();
+  const uint32_t tbase = *slot;
+  const uint32_t s0 = smem_u32(sm);
+  const uint32_t tl = tbase + ((uint32_t)((warp & 3) * 32) << 16);     // epilogue warps 0-3: lanes 32w .. 32w+31
+  volatile int* ab = abort_;
+  uint32_t parity = 0;
+  bool stop = false;
+
+  for (int64_t i = blockIdx.x; i < N && !stop; i += gridDim.x) {
+    const int64_t e0 = row_ptr[i];
+    const int deg = row_ptr[i + 1] - (int)e0;
+    for (int c0 = 0; c0 < deg; c0 += kARows) {
+      const int nrow = min(kARows, deg - c0);
+      __syncthreads();                       // the previous chunk's MMAs are complete and its TMEM reads done
+      fence_after_sync();
+      if (*ab) {                             // uniform: the flag is written only before a barrier
+        stop = true;
+        break;
+      }
+      if (c0 == 0) stage_g(sm, G, i, tid);
+      // A operands (padding rows zero) and this row's epilogue inputs
+      float yv[kAX], pv[kAB];
+      const bool valid = tid < nrow;
+      const int64_t e = e0 + c0 + tid;
+      if (tid < kARows) {
+        const float4 z4 = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+        for (int k = 0; k < kAK; k += 4) {
+          const float4 v = valid ? __ldg(reinterpret_cast<const float4*>(msg + e * kAK + k)) : z4;
+          store_split4(sm + oAMh, sm + oAMl, kmajor_off(tid, k, kARows), v.x, v.y, v.z, v.w);
+        }
+#pragma unroll
+        for (int b = 0; b < kAB; b += 4) {
+          const float4 v = valid ? __ldg(reinterpret_cast<const float4*>(phi + e * kAB + b)) : z4;
+          pv[b] = v.x; pv[b + 1] = v.y; pv[b + 2] = v.z; pv[b + 3] = v.w;
+          store_split4(sm + oAPh, sm + oAPl, kmajor_off(tid, b, kARows), v.x, v.y, v.z, v.w);
+        }
+#pragma unroll
+        for (int x = 0; x < kAX; x += 4) {
+          const float4 v = valid ? __ldg(reinterpret_cast<const float4*>(Y + e * kAX + x)) : z4;
+          yv[x] = v.x; yv[x + 1] = v.y; yv[x + 2] = v.z; yv[x + 3] = v.w;
+        }
+      }
+      fence_proxy_async_smem();
+      fence_before_sync();
+      __syncthreads();
+      // ---- phase 1: T -> columns [0, 320), U (x < 5) -> [320, 480)
+      if (tid == kARows) {
+        fence_after_sync();
+        mma_split(tbase, s0 + oAMh, s0 + oAMl, s0 + oBTh, s0 + oBTl, kANT, 0, kAK / 8);
+        mma_split(tbase + kAN, s0 + oAMh, s0 + oAMl, s0 + oBTh, s0 + oBTl, kANT, kAN, kAK / 8);
+        mma_split(tbase + 2 * kAN, s0 + oAPh, s0 + oAPl, s0 + oBUh, s0 + oBUl, kANU, 0, kAB / 8);
+        commit(mbar);
+      }
+      float dm[kAK];
+      if (warp < 4) {
+        float dp[kAB], dyv[kAX];
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(mbar, parity, ab) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        fence_after_sync();
+#pragma unroll
+        for (int b = 0; b < kAB; b++) dp[b] = 0.f;
+#pragma unroll
+        for (int k = 0; k < kAK; k++) dm[k] = 0.f;
+        if (ok) {
+#pragma unroll
+          for (int x = 0; x < kAX; x += 2) {              // T rows (x, b), two x per pair of loads
+            float t[32];
+            tmem_ld32(tl + x * kAB, t);
+#pragma unroll
+            for (int h = 0; h < 2; h++) {
+              float s = 0.f;
+#pragma unroll
+              for (int b = 0; b < kAB; b++) {
+                s += pv[b] * t[h * kAB + b];
+                dp[b] += yv[x + h] * t[h * kAB + b];
+              }
+              dyv[x + h] = s;
+            }
+          }
+          if (valid) {                                     // dphi, dY are complete after phase 1
+#pragma unroll
+            for (int b = 0; b < kAB; b += 4)
+              *reinterpret_cast<float4*>(dphi + e * kAB + b) = make_float4(dp[b], dp[b + 1], dp[b + 2], dp[b + 3]);
+#pragma unroll
+            for (int x = 0; x < kAX; x += 4)
+              *reinterpret_cast<float4*>(dY + e * kAX + x) = make_float4(dyv[x], dyv[x + 1], dyv[x + 2], dyv[x + 3]);
+          }
+#pragma unroll
+          for (int x = 0; x < 5; x++) {                    // U rows (x, k), x < 5
+            float u[32];
+            tmem_ld32(tl + 2 * kAN + x * kAK, u);
+#pragma unroll
+            for (int k = 0; k < kAK; k++) dm[k] += yv[x] * u[k];
+          }
+        }
+      }
+      parity ^= 1u;
+      fence_before_sync();
+      __syncthreads();
+      if (*ab) {
+        stop = true;
+        break;
+      }
+      // ---- phase 2: U (x >= 5) -> columns [0, 480)
+      if (tid == kARows) {
+        fence_after_sync();
+        for (int q = 1; q < 4; q++)
+          mma_split(tbase + (q - 1) * kAN, s0 + oAPh, s0 + oAPl, s0 + oBUh, s0 + oBUl, kANU, q * kAN, kAB / 8);
+        commit(mbar);
+      }
+      if (warp < 4) {
+        int ok = 1;
+        if (lane == 0) ok = mbar_wait(mbar, parity, ab) ? 1 : 0;
+        ok = __shfl_sync(0xffffffffu, ok, 0);
+        fence_after_sync();
+        if (ok) {
+#pragma unroll
+          for (int x = 5; x < kAX; x++) {
+            float u[32];
+            tmem_ld32(tl + (x - 5) * kAK, u);
+#pragma unroll
+            for (int k = 0; k < kAK; k++) dm[k] += yv[x] * u[k];
+          }
+          if (valid) {
+#pragma unroll
+            for (int k = 0; k < kAK; k += 4)
+              *reinterpret_cast<float4*>(dmsg + e * kAK + k) = make_float4(dm[k], dm[k + 1], dm[k + 2], dm[k + 3]);
+          }
+        }
+      }
+      parity ^= 1u;
+      fence_before_sync();
+    }
+  }
+  __syncthreads();
+  fence_after_sync();
+  if (warp == 0) tmem_dealloc(tbase, 512);
+}
+
+}  // namespace
+
+int density_tc_xm_bwd(const float* phi, const float* msg, const float* Y, const float* const G[4], float* dphi,
+                      float* dmsg, float* dY, int64_t N, const int32_t* row_ptr, void* stream) {
+  if (N == 0) return FACEK_OK;
+  FACEK_CHECK_ARG((int)kASmem <= max_smem_optin(), "facek_density_tc_xm_bwd: needs %u B of shared memory", kASmem);
+  const uintptr_t al = reinterpret_cast<uintptr_t>(phi) | reinterpret_cast<uintptr_t>(msg) |
+                       reinterpret_cast<uintptr_t>(Y) | reinterpret_cast<uintptr_t>(dphi) |
+                       reinterpret_cast<uintptr_t>(dmsg) | reinterpret_cast<uintptr_t>(dY) |
+                       reinterpret_cast<uintptr_t>(G[0]) | reinterpret_cast<uintptr_t>(G[1]) |
+                       reinterpret_cast<uintptr_t>(G[2]) | reinterpret_cast<uintptr_t>(G[3]);
+  FACEK_CHECK_ARG((al & 15) == 0, "facek_density_tc_xm_bwd: tensors must be 16-byte aligned");
+  GPlanes P{{G[0], G[1], G[2], G[3]}, N * (int64_t)(kAB * kAK), (int64_t)(kAB * kAK)};
+  cudaFuncSetAttribute(dens_bwd_tc_k, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)kASmem);
+  dens_bwd_tc_k<<<grid_for(N, 1), kAThreads, kASmem, as_stream(stream)>>>(phi, msg, Y, P, dphi, dmsg, dY, N,
+                                                                          row_ptr);
+  return launch_status("facek_density_tc_xm_bwd");
+}
+
 int density_tc_status(int clear) {
   int v = 0;
   if (cudaMemcpyFromSymbol(&v, tc::g_tc_status, sizeof(int)) != cudaSuccess) return -1;
@@ -349,4 +627,19 @@ extern "C" int facek_density_tc_xm_fwd(const float* phi, const float* msg, const
   FACEK_CHECK_ARG(N >= 0 && B == 16 && K == 32 && row_ptr && D && (N == 0 || (phi && msg && Y)),
                   "facek_density_tc_xm_fwd: needs B = 16, K = 32 and non-null tensors (got B=%d K=%d)", B, K);
   return density_tc_xm_fwd(phi, msg, Y, D, N, row_ptr, stream);
+}
+
+extern "C" int facek_density_msg_tc_xm_bwd(const float* phi, const float* msg, const float* Y, const float* G0,
+                                           const float* G1, const float* G2, const float* G3, const float* TJ,
+                                           const float* TI, const int32_t* ei, const int32_t* ej, int32_t nc,
+                                           float* dphi, float* dmsg, float* dY, int64_t N, int64_t E, int32_t B,
+                                           int32_t K, const int32_t* row_ptr, void* stream) {
+  FACEK_CHECK_ARG(N >= 0 && E >= 0 && B == 16 && K == 32 && nc >= 1 && nc <= 10 && row_ptr && G0 && G1 && G2 && G3 &&
+                      TJ && ei && ej && (E == 0 || (phi && msg && Y && dphi && dmsg && dY)),
+                  "facek_density_msg_tc_xm_bwd: bad arguments (fp32, B = 16, K = 32 only)");
+  if (N == 0) return FACEK_OK;
+  const float* G[4] = {G0, G1, G2, G3};
+  int st = density_tc_xm_bwd(phi, msg, Y, G, dphi, dmsg, dY, N, row_ptr, stream);
+  if (st) return st;
+  return edge_msg_dy(FACEK_F32, ei, ej, TJ, TI, dmsg, nc, K, N, E, dY, stream);
 }

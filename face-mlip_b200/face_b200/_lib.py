@@ -45,6 +45,7 @@ SIGNATURES = {
     "facek_radial_fwd": [I32, P, P, P, P, I32, D, I32, I32, I32, P, P, P, P, P, P, P, P, P, I64, P],
     "facek_density_tc_xm_fwd": [P, P, P, P, I64, I32, I32, P, P],
     "facek_density_msg_xm_bwd": [I32, P, P, P, P, P, P, P, P, P, P, P, I32, P, P, P, I64, I64, I32, I32, P, P],
+    "facek_density_msg_tc_xm_bwd": [P, P, P, P, P, P, P, P, P, P, P, I32, P, P, P, I64, I64, I32, I32, P, P],
     "facek_radial_simt_fwd": [I32, P, P, P, P, I32, D, I32, I32, I32, P, P, P, P, P, P, P, P, P, I64, P],
     "facek_radial_tc_fwd": [P, P, P, P, I32, D, I32, I32, I32, P, P, P, P, P, P, P, P, P, I64, P],
     "facek_tc_status": [P, I32],

@@ -17,6 +17,7 @@ is one contiguous (k_l*N, channels) GEMM operand and no autograd slice ever zero
                once to that order (face/model.py:525-533)
 """
 import math
+import os
 
 import numpy as np
 import torch
@@ -28,6 +29,9 @@ from .neighbors import graph_from_padded
 KE = 14.399645                                      # face/electrostatics.py:20
 Y2W = (1.0, 1.0, 1.0, 2.0, 2.0, 2.0)                # face/cartesian.py:81
 RANK = [(0, 1), (1, 4), (4, 10), (10, 20)]
+# density adjoint of the fp32 B=16 K=32 shape on the tensor cores (facek_density_msg_tc_xm_bwd) instead of the
+# lane-per-edge CUDA-core kernel (facek_density_msg_xm_bwd)
+DENSITY_ADJOINT_TC = os.environ.get("FACEK_DENSITY_ADJOINT", "simt") == "tc"
 
 
 def _p(t):
@@ -205,9 +209,14 @@ class DensityMsg(torch.autograd.Function):
         G = [g.contiguous() if g is not None else torch.zeros(b - a, N, B * K, dtype=phi.dtype, device=phi.device)
              for g, (a, b) in zip(dD, RANK)]
         dphi, dmsg, dY = torch.empty_like(phi), torch.empty_like(msg), torch.empty_like(Y)
-        _lib.call("facek_density_msg_xm_bwd", _tag(phi), _p(phi), _p(msg), _p(Y), *[_p(g) for g in G], _p(TJ), _p(TI),
-                  _p(gr["ei"]), _p(gr["ej"]), nc, _p(dphi), _p(dmsg), _p(dY), N, E, B, K, _p(gr["row_ptr"]),
-                  _lib.stream())
+        if DENSITY_ADJOINT_TC and phi.dtype == torch.float32 and B == 16 and K == 32:
+            _lib.call("facek_density_msg_tc_xm_bwd", _p(phi), _p(msg), _p(Y), *[_p(g) for g in G], _p(TJ), _p(TI),
+                      _p(gr["ei"]), _p(gr["ej"]), nc, _p(dphi), _p(dmsg), _p(dY), N, E, B, K, _p(gr["row_ptr"]),
+                      _lib.stream())
+        else:
+            _lib.call("facek_density_msg_xm_bwd", _tag(phi), _p(phi), _p(msg), _p(Y), *[_p(g) for g in G], _p(TJ),
+                      _p(TI), _p(gr["ei"]), _p(gr["ej"]), nc, _p(dphi), _p(dmsg), _p(dY), N, E, B, K,
+                      _p(gr["row_ptr"]), _lib.stream())
         dTJ = torch.empty_like(TJ)
         dTI = torch.empty_like(TI) if TI is not None else None
         _lib.call("facek_edge_msg_bwd", _tag(Y), _p(Y), _p(gr["ei"]), _p(gr["ej"]), _p(TJ), _p(TI), _p(dmsg),

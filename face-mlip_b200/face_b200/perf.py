@@ -11,7 +11,8 @@ Per launch, the ALGORITHMIC bytes (each input read once, each output written onc
   channel GEMM      facek_gemm_tc             bytes  4*rows*(K + N*(1+beta)) + 8*K*N (split weight image)
                                               flops  2*rows*K*N
 
-(e = element size, E edges, N atoms.)  Each kernel is reported against the measured HBM copy bandwidth and against
+(e = element size, E edges, N atoms; the tensor-core density adjoint facek_density_msg_tc_xm_bwd has the same
+algorithmic bytes and FLOPs as the CUDA-core one.)  Each kernel is reported against the measured HBM copy bandwidth and against
 the FP32 SIMT peak (148 SMs x 128 FP32 lanes x 2 FLOP x the maximum SM clock); the attainable fraction is
 max(bytes / HBM, flops / FP32 peak) / measured time, the roofline of a kernel that both streams and computes.
 The GEMM runs on the tensor cores with a 3-term TF32 split; its attainable bound is HBM.
@@ -24,9 +25,11 @@ from . import _lib
 
 SMS, FP32_LANES = 148, 128
 
-ENTRIES = {"dens_bwd": "facek_density_msg_xm_bwd", "gemm": "facek_gemm_tc", "dens_fwd": "facek_density_xm_fwd"}
-KERNEL_NAMES = {"dens_bwd": "dens_bwd_lane_k (facek_density_msg_xm_bwd)", "gemm": "gemm_tc_k (facek_gemm_tc)",
-                "dens_fwd": "dens_fwd_k (facek_density_xm_fwd)"}
+ENTRIES = {"dens_bwd": "facek_density_msg_xm_bwd", "dens_bwd_tc": "facek_density_msg_tc_xm_bwd",
+           "gemm": "facek_gemm_tc", "dens_fwd": "facek_density_xm_fwd"}
+KERNEL_NAMES = {"dens_bwd": "dens_bwd_lane_k (facek_density_msg_xm_bwd)",
+                "dens_bwd_tc": "dens_bwd_tc_k + message dY (facek_density_msg_tc_xm_bwd)",
+                "gemm": "gemm_tc_k (facek_gemm_tc)", "dens_fwd": "dens_fwd_k (facek_density_xm_fwd)"}
 
 
 def peaks(root):
@@ -50,8 +53,8 @@ def start():
 def _sizes(name, args, E, N, B, K, esz):
     if name == "facek_density_xm_fwd":
         return (esz * E * (B + K + 20) + esz * N * 20 * B * K + 4 * (N + 1), 2.0 * E * 20 * B * K)
-    if name == "facek_density_msg_xm_bwd":
-        nc = int(args[12])
+    if name in ("facek_density_msg_xm_bwd", "facek_density_msg_tc_xm_bwd"):
+        nc = int(args[12] if name == "facek_density_msg_xm_bwd" else args[11])
         return (esz * N * 20 * B * K + 2 * esz * E * (B + K + 20) + 2 * esz * nc * N * K + 4 * (N + 1) + 8 * E,
                 2.0 * E * (40 * B * K + 40 * B + 2 * nc * K))
     if name == "facek_gemm_tc":

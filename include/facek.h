@@ -60,6 +60,16 @@ int facek_density_msg_xm_bwd(int dtype, const void* phi, const void* msg, const 
                              const void* G1, const void* G2, const void* G3, const void* TJ, const void* TI,
                              const int32_t* ei, const int32_t* ej, int32_t nc, void* dphi, void* dmsg, void* dY,
                              int64_t N, int64_t E, int32_t B, int32_t K, const int32_t* row_ptr, void* stream);
+/* The same outputs on the tcgen05 tensor cores (fp32, B = 16, K = 32 only; no reference counterpart as a C entry
+ * point, face/kernels.py:56-118): per atom and chunk of up to 128 edges, T[e,(x,b)] = msg[e,:] . G[x,b,:] and
+ * U[e,(x,k)] = phi[e,:] . G[x,:,k] as two MMAs with the edges as M (3-term tf32 split), then dphi, dY and dmsg from
+ * T and U on the CUDA cores; the message part of dY follows as in facek_edge_msg_bwd.  Needs 16-byte aligned
+ * tensors and ~208 KB of opt-in shared memory.  Same outputs to fp32 accuracy; at present slower than
+ * facek_density_msg_xm_bwd on the cfg5 alloy (operand staging bound), so the engine keeps the CUDA-core kernel. */
+int facek_density_msg_tc_xm_bwd(const float* phi, const float* msg, const float* Y, const float* G0, const float* G1,
+                                const float* G2, const float* G3, const float* TJ, const float* TI, const int32_t* ei,
+                                const int32_t* ej, int32_t nc, float* dphi, float* dmsg, float* dY, int64_t N,
+                                int64_t E, int32_t B, int32_t K, const int32_t* row_ptr, void* stream);
 
 /* ---------------------------------------------------------------------------------------------------
  * Node invariant algebra, reference layout.  Replaces face-mlip face/node_kernel.py:18-64 (node_fwd) and

@@ -281,6 +281,54 @@ def test_density_msg_fused_matches_composed(small_graph, dt, nc):
         assert rel(a.double(), b.double()) < tol
 
 
+@pytest.mark.parametrize("rows", ["alloy", "long_rows"])
+@pytest.mark.parametrize("nc", [1, 10])
+def test_density_adjoint_tensor_core(small_graph, rows, nc):
+    """facek_density_msg_tc_xm_bwd (tcgen05, edges as M) against the float64 CUDA-core adjoint on the same inputs:
+    dphi, dmsg, dY with the message part.  "long_rows": rows of 130-300 edges (chunks of 128 edges of one atom)
+    and empty rows.  Bar: 4x the error of the fp32 CUDA-core kernel against float64 (and at most 2e-5 relative)."""
+    from face_b200 import _lib
+    if rows == "alloy":
+        rp = small_graph["row_ptr"].long()
+        ei, ej = small_graph["ei"], small_graph["ej"]
+    else:
+        deg = torch.tensor([130, 0, 300, 7, 0, 256, 129, 45], device=DEV)
+        rp = torch.zeros(deg.numel() + 1, dtype=torch.long, device=DEV)
+        rp[1:] = torch.cumsum(deg, 0)
+        ei = torch.repeat_interleave(torch.arange(deg.numel(), device=DEV), deg).int()
+        ej = torch.randint(0, deg.numel(), (int(rp[-1]),), device=DEV).int()
+    N, E = rp.numel() - 1, int(rp[-1])
+    torch.manual_seed(13)
+    r64 = lambda *sh: torch.randn(*sh, device=DEV, dtype=torch.float64)
+    phi, msg, Y = r64(E, 16), r64(E, 32), r64(E, 20)
+    G = [r64(k, N, 512) for k in (1, 3, 6, 10)]
+    TJ, TI = r64(nc, N, 32), r64(nc, N, 32)
+    row_ptr = rp.int().contiguous()
+
+    def run(dt, tc):
+        a = [t.to(dt).contiguous() for t in (phi, msg, Y)]
+        gg = [t.to(dt).contiguous() for t in G]
+        tj, ti = TJ.to(dt).contiguous(), TI.to(dt).contiguous()
+        out = [torch.empty_like(a[0]), torch.empty_like(a[1]), torch.empty_like(a[2])]
+        if tc:
+            _lib.call("facek_density_msg_tc_xm_bwd", *[_lib.ptr(t) for t in a], *[_lib.ptr(t) for t in gg],
+                      _lib.ptr(tj), _lib.ptr(ti), _lib.ptr(ei), _lib.ptr(ej), nc, *[_lib.ptr(t) for t in out], N, E,
+                      16, 32, _lib.ptr(row_ptr), _lib.stream())
+        else:
+            _lib.call("facek_density_msg_xm_bwd", _lib.dtype_tag(a[0]), *[_lib.ptr(t) for t in a],
+                      *[_lib.ptr(t) for t in gg], _lib.ptr(tj), _lib.ptr(ti), _lib.ptr(ei), _lib.ptr(ej), nc,
+                      *[_lib.ptr(t) for t in out], N, E, 16, 32, _lib.ptr(row_ptr), _lib.stream())
+        return [t.double() for t in out]
+
+    ref, simt, tc = run(torch.float64, False), run(torch.float32, False), run(torch.float32, True)
+    st = _lib.ctypes.c_int32(0)
+    _lib.call("facek_tc_status", _lib.ctypes.byref(st), 1)
+    assert st.value == 0, "tensor-core wait ran out"
+    for name, r, a, b in zip(("dphi", "dmsg", "dY"), ref, simt, tc):
+        e_simt, e_tc = rel(a, r), rel(b, r)
+        assert e_tc <= max(4 * e_simt, 1e-7) and e_tc < 2e-5, (name, e_tc, e_simt)
+
+
 def test_transport_fp64(small_graph):
     from face_b200.ops import EdgeVec, Transport
     g = small_graph
