@@ -180,9 +180,16 @@ def run_ours(a):
     g = build_graph(structs, spec["rc"], device=dev, dtype=dtype)
     E = int(g["ei"].numel())
 
-    def step():
-        gg = dict(g, pos=g["pos"].detach().clone())
-        return model(gg)["forces"]
+    if a.graph:                                   # the whole evaluation as one CUDA-graph replay (face_b200.graphs)
+        from face_b200.graphs import GraphedEvaluation
+        ev = GraphedEvaluation(model, g)
+
+        def step():
+            return ev(g["pos"])["forces"]
+    else:
+        def step():
+            gg = dict(g, pos=g["pos"].detach().clone())
+            return model(gg)["forces"]
 
     t0 = time.perf_counter()
     for _ in range(a.warmup):
@@ -205,7 +212,7 @@ def run_ours(a):
         e1.record()
         torch.cuda.synchronize()
     _lib.COUNTING = False
-    launches = _lib.launches()
+    launches = ev.launches * a.steps if a.graph else _lib.launches()
     ms = e0.elapsed_time(e1) / a.steps
     kernel_ms = {k[6:]: round(sum(s.elapsed_time(t) for s, t in v) / a.steps, 3) for k, v in _lib.TIMED.items() if v}
     value = natoms * a.steps / (e0.elapsed_time(e1) / 1e3)
@@ -242,7 +249,7 @@ def run_ours(a):
                                                          f"BASELINE configuration {a.config}, scale {a.scale}"),
                       "atoms": natoms, "edges": E, "l2": ("inputs larger than L2 (edge tensors of several GB)" if E * 4 * 20 > 126e6 else
                              "small workload: edge tensors fit in L2, not flushed between steps"),
-                      "parallelism": "single GPU"},
+                      "parallelism": "single GPU", "cuda_graph": bool(a.graph)},
            "e2e": e2e,
            "roofline": perf.headline(rows, pk),
            "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
@@ -275,6 +282,7 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--graph", action="store_true", help="single GPU: each step one CUDA-graph replay of the evaluation")
     ap.add_argument("--scale", type=int, default=None,
                     help="smaller system of the same configuration (cfg5: conventional cells per side), for profiling")
     a = ap.parse_args()

@@ -72,11 +72,12 @@ class FACECalculator(Calculator):
     list of pairs closer than rc + skin across calls while no atom has moved more than skin/2 since it was built
     (and species, cell and periodicity are unchanged), as MD drivers do (face/neighbors.py:7 builds such lists).
     The model's envelope is zero beyond rc and the Coulomb real-space sum is cut at rc, so a reused list gives the
-    same energies and forces as a fresh one.  The reuse test costs one device-side max and one scalar read."""
+    same energies and forces as a fresh one.  The reuse test costs one device-side max and one scalar read.
+    `cuda_graph` replays one captured CUDA graph per evaluation while the list is reused (face_b200.graphs)."""
     implemented_properties = ["energy", "forces"]
 
     def __init__(self, path=None, device="cuda", fused=True, e_shift=0.0, model=None, dtype=torch.float32, skin=0.0,
-                 **kw):
+                 cuda_graph=False, **kw):
         super().__init__(**kw)
         if model is None:
             model, ck = load_face(path, device)
@@ -87,6 +88,10 @@ class FACECalculator(Calculator):
         self.skin = float(skin)
         self._graph, self._key, self._stage = None, None, None
         self.rebuilds = 0
+        # cuda_graph: each evaluation on a reused neighbour list is one CUDA-graph replay (face_b200.graphs), captured
+        # again after every rebuild; worthwhile with a skin, for systems small enough to be launch-bound
+        self.cuda_graph = bool(cuda_graph)
+        self._replay, self._replay_of = None, None
 
     def _positions(self, pos):
         """Host positions -> device float64 through a pinned staging buffer."""
@@ -114,7 +119,16 @@ class FACECalculator(Calculator):
     def calculate(self, atoms=None, properties=("energy",), system_changes=all_changes):
         super().calculate(atoms, properties, system_changes)
         at = self.atoms if atoms is None else atoms
-        o = self.model(self.graph(at))
+        g = self.graph(at)
+        if self.cuda_graph:
+            from .graphs import GraphedEvaluation
+            if self._replay_of is not self._graph:
+                self._replay = None                        # release the previous capture before the next one
+                self._replay = GraphedEvaluation(self.model, self._graph)
+                self._replay_of = self._graph
+            o = self._replay(g["pos"])
+        else:
+            o = self.model(g)
         self.results["energy"] = float(o["energy"].item()) + self.e_shift
         self.results["forces"] = o["forces"].detach().double().cpu().numpy()
 

@@ -73,3 +73,47 @@ def test_calculator_skin_reuse_matches_fresh_lists(dtype):
         assert abs(e1 - e0) <= tol_e * abs(e0), (step, e0, e1)
         assert np.abs(f1 - f0).max() <= tol_f, step
     assert fresh.rebuilds == 8 and 1 < reuse.rebuilds < 8, reuse.rebuilds
+
+
+@pytest.mark.parametrize("case", ["molecules", "periodic_coulomb"])
+def test_graphed_evaluation_matches_eager(case):
+    """One captured CUDA graph of the whole forward + force backward (face_b200.graphs), replayed at new positions,
+    against the eager evaluation at the same positions (fp32; PME spreads with atomics, so not bit for bit)."""
+    from face_b200 import systems
+    from face_b200.graphs import GraphedEvaluation
+    from face_b200.neighbors import build_graph
+    if case == "molecules":
+        m, rc = _model(3, torch.float32)
+        structs = systems.config_structures(3, seed=1, scale=6)
+    else:
+        m, rc = _model(2, torch.float32, pme={"gp": 1 / 0.32, "mesh": (24, 24, 24)})
+        structs = [systems.rocksalt(3, 5.64, 0.05, seed=2)]
+    g = build_graph(structs, rc, dtype=torch.float32, skin=0.5)
+    ev = GraphedEvaluation(m, g)
+    gen = torch.Generator(device="cuda").manual_seed(0)
+    for _ in range(3):
+        pos = g["pos"] + 0.05 * torch.randn(g["pos"].shape, device="cuda", generator=gen)
+        o1 = ev(pos)
+        o2 = m(dict(g, pos=pos.clone()))
+        assert float((o1["energy"] - o2["energy"]).abs().max()) <= 1e-6 * float(o2["energy"].abs().max())
+        assert float((o1["forces"] - o2["forces"]).abs().max()) <= 1e-5
+
+
+def test_calculator_cuda_graph_with_skin():
+    """The calculator with a skin and CUDA-graph replays (recaptured at every rebuild) against fresh eager lists."""
+    from face_b200 import systems
+    from face_b200.calculator import FACECalculator
+    m, rc = _model(3, torch.float32, seed=2)
+    mol = systems.molecule(30, seed=9)
+    fresh = FACECalculator(model=m, device="cuda", dtype=torch.float32)
+    graphed = FACECalculator(model=m, device="cuda", dtype=torch.float32, skin=1.0, cuda_graph=True)
+    rng = np.random.default_rng(1)
+    pos = mol.positions.copy()
+    for step in range(6):
+        pos = pos + rng.normal(0, 0.1, pos.shape)
+        at = systems.Structure(pos.copy(), mol.numbers)
+        fresh.calculate(at)
+        graphed.calculate(at)
+        assert abs(graphed.results["energy"] - fresh.results["energy"]) <= 1e-6 * abs(fresh.results["energy"]) + 1e-6
+        assert np.abs(graphed.results["forces"] - fresh.results["forces"]).max() <= 1e-4
+    assert 1 <= graphed.rebuilds < 6
