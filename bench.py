@@ -176,6 +176,8 @@ def run_ours(a):
     if a.scale and a.config == 5:                           # keep the PME grid spacing of the full box
         pme["mesh"] = tuple(max(8, int(round(n * a.scale / 64))) for n in pme["mesh"])
     model = make_model(spec, pme, dev, dtype)
+    if a.compiled_radial:                         # the reference's inference mode (fused + compiled radial)
+        model.compile_radial()
     natoms = sum(len(s.numbers) for s in structs)
     g = build_graph(structs, spec["rc"], device=dev, dtype=dtype)
     E = int(g["ei"].numel())
@@ -249,7 +251,8 @@ def run_ours(a):
                                                          f"BASELINE configuration {a.config}, scale {a.scale}"),
                       "atoms": natoms, "edges": E, "l2": ("inputs larger than L2 (edge tensors of several GB)" if E * 4 * 20 > 126e6 else
                              "small workload: edge tensors fit in L2, not flushed between steps"),
-                      "parallelism": "single GPU", "cuda_graph": bool(a.graph)},
+                      "parallelism": "single GPU", "cuda_graph": bool(a.graph),
+                      "radial": "compiled (cubic Hermite tables)" if a.compiled_radial else "MLP"},
            "e2e": e2e,
            "roofline": perf.headline(rows, pk),
            "cpu_baseline": cpu, "clocks": clk.summary(), "gpu_launches": launches,
@@ -282,6 +285,8 @@ def main():
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-cpu", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=12.0)
+    ap.add_argument("--compiled-radial", action="store_true",
+                    help="radial MLP replaced by its per-pair spline tables, the reference's inference mode")
     ap.add_argument("--graph", action="store_true", help="single GPU: each step one CUDA-graph replay of the evaluation")
     ap.add_argument("--scale", type=int, default=None,
                     help="smaller system of the same configuration (cfg5: conventional cells per side), for profiling")

@@ -67,7 +67,8 @@ def load_face(path, device="cuda"):
 class FACECalculator(Calculator):
     """Energy and forces of one atoms object (face/calculator.py:35-55).
 
-    `fused` is accepted for the reference's signature and ignored: the engine has only its CUDA path.
+    `fused` (default True) compiles the radial MLP of a checkpoint-loaded model into its cubic Hermite tables, as the
+    reference's calculator does (face/calculator.py:42-44); the engine has only its CUDA path otherwise.
     `skin` (Angstrom, default 0 = the reference's behaviour, a fresh neighbour list every call) keeps the neighbour
     list of pairs closer than rc + skin across calls while no atom has moved more than skin/2 since it was built
     (and species, cell and periodicity are unchanged), as MD drivers do (face/neighbors.py:7 builds such lists).
@@ -82,6 +83,8 @@ class FACECalculator(Calculator):
         if model is None:
             model, ck = load_face(path, device)
             e_shift = e_shift + float(ck.get("Eref", 0.0))
+            if fused and torch.device(device).type == "cuda" and model.form != "moment" and model.spline[0] is None:
+                model.compile_radial()                    # as the reference's calculator does (face/calculator.py:42-44)
         self.model = model.to(device=device, dtype=dtype)
         self.device, self.dtype = device, dtype
         self.e_shift = e_shift
