@@ -158,8 +158,36 @@ __global__ void __launch_bounds__(kThreads, 1)
 
   const float cb = sqrtf(2.f / rc);
   const float pi = 3.14159265358979323846f;
+  const float th = pi / rc;
   const int64_t ntiles = (E + kRows - 1) / kRows;
-  for (int64_t t = (int64_t)blockIdx.x * 2 + wg; t < ntiles; t += (int64_t)gridDim.x * 2) {
+  const int64_t tstride = (int64_t)gridDim.x * 2;
+  // the next tile's edge geometry and element pair, loaded one tile ahead (ei/ej at the start of the previous
+  // tile, zidx after its layer 1), so the dependent ei -> zidx chain is off the critical path
+  float nx = 0.f, ny = 0.f, nz = 0.f;
+  int ni = 0, nj = 0;
+  auto fetch_geom = [&](int64_t tt) {
+    const int64_t ee = tt * kRows + row;
+    if (tt < ntiles && ee < E) {
+      nx = vec[ee * 3];
+      ny = vec[ee * 3 + 1];
+      nz = vec[ee * 3 + 2];
+      ni = ei[ee];
+      nj = ej[ee];
+    }
+  };
+  auto fetch_elem = [&](int64_t tt) {
+    const int64_t ee = tt * kRows + row;
+    if (tt < ntiles && ee < E) {
+      ni = zidx[ni];
+      nj = zidx[nj];
+    }
+  };
+  {
+    const int64_t t0 = (int64_t)blockIdx.x * 2 + wg;
+    fetch_geom(t0);
+    fetch_elem(t0);
+  }
+  for (int64_t t = (int64_t)blockIdx.x * 2 + wg; t < ntiles; t += tstride) {
     bar_sync(1 + wg, 2 * kRows);
     if (*ab) break;                                  // uniform: nothing writes the flag between these points
     const int64_t e = t * kRows + row;
@@ -167,55 +195,74 @@ __global__ void __launch_bounds__(kThreads, 1)
     float r = 0.5f * rc;
     int p = 0;
     if (valid) {
-      const float vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
-      r = sqrtf(vx * vx + vy * vy + vz * vz);
-      p = zidx[ei[e]] * n_el + zidx[ej[e]];
+      r = sqrtf(nx * nx + ny * ny + nz * nz);
+      p = ni * n_el + nj;
     }
+    fetch_geom(t + tstride);
     float env, denv;
     envelope(r, rc, env, denv);
+    // Bessel basis sqrt(2/rc) sin(f_n r)/r, f_n = (n+1) pi/rc, by the angle-addition recurrence
+    //   sin((n+2) x) = sin((n+1) x) cos x + cos((n+1) x) sin x,  cos((n+2) x) = cos((n+1) x) cos x - sin((n+1) x) sin x
+    // restarted from a direct sincos every 4 terms (fp32 error <= 3e-7 absolute, below the argument rounding of a
+    // direct sin(f_n r) at n ~ 16)
+    const float ir = 1.f / r, cbr = cb * ir;
     float rb[NB], drb[NB];
+    {
+      float s1, c1;
+      sincosf(th * r, &s1, &c1);
+      float sn = s1, cn = c1;
 #pragma unroll
-    for (int n = 0; n < NB; n++) {
-      rb[n] = 0.f;
-      drb[n] = 0.f;
-      if (n < nb) {
-        const float f = float(n + 1) * pi / rc;
-        const float s = sinf(f * r), co = cosf(f * r);
-        const float bes = s / r * cb;
-        const float dbes = (f * co / r - s / (r * r)) * cb;
-        rb[n] = bes * env;
-        drb[n] = dbes * env + bes * denv;
+      for (int n = 0; n < NB; n++) {
+        if (n > 0 && n % 4 == 0) sincosf(float(n + 1) * th * r, &sn, &cn);
+        const float f = float(n + 1) * th;
+        const float bes = sn * cbr;
+        const float dbes = (f * cn - sn * ir) * cbr;
+        rb[n] = n < nb ? bes * env : 0.f;
+        drb[n] = n < nb ? dbes * env + bes * denv : 0.f;
+        const float s2 = sn * c1 + cn * s1;
+        cn = cn * c1 - sn * s1;
+        sn = s2;
       }
     }
-    // ---- layer 1 on the CUDA cores (this thread's 32 hidden units): a1 -> operand planes, da1 in registers
+    // ---- layer 1 on the CUDA cores (this thread's 32 hidden units): a1 -> operand planes, da1 parked in this
+    // lane's TMEM columns [128 + h) (free while round 1 writes [0, 128))
     const float* pcol = pairs + p;
     constexpr int kHh = kH / 2;
-    float da1[kHh];
-#pragma unroll
-    for (int hh = 0; hh < kHh; hh += 4) {
+    const uint32_t park = tl + 128 + half * kHh;
+#pragma unroll 1
+    for (int hh = 0; hh < kHh; hh += 8) {
       const int h0 = half * kHh + hh;
-      float a[4];
+      float a[8], da[8];
 #pragma unroll
-      for (int j = 0; j < 4; j++) {
+      for (int j = 0; j < 8; j++) {
         const int h = h0 + j;
         float z = pcol[h * np], dz = 0.f;
 #pragma unroll
         for (int n = 0; n < NB; n++) ffma2(z, dz, w1s[h * NB + n], w1s[h * NB + n], rb[n], drb[n]);
         const float sg = sigmoid_f(z);
         a[j] = z * sg;
-        da1[hh + j] = sg * (1.f + z * (1.f - sg)) * dz;
+        da[j] = sg * (1.f + z * (1.f - sg)) * dz;
       }
       store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), a[0], a[1], a[2], a[3]);
+      store_split4(a_hi, a_lo, kmajor_off(row, h0 + 4, kRows), a[4], a[5], a[6], a[7]);
+      tmem_st8(park + hh, da);
     }
+    fetch_elem(t + tstride);
+    tmem_wait_st();
     round(col0, w2_s, kH);                                                   // z2 -> columns [0, 128)
 #pragma unroll
-    for (int hh = 0; hh < kHh; hh += 4)
-      store_split4(a_hi, a_lo, kmajor_off(row, half * kHh + hh, kRows), da1[hh], da1[hh + 1], da1[hh + 2],
-                   da1[hh + 3]);
+    for (int hh = 0; hh < kHh; hh += 8) {
+      float v[8];
+      tmem_ld8(park + hh, v);
+      tmem_wait_ld();
+      const int h0 = half * kHh + hh;
+      store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), v[0], v[1], v[2], v[3]);
+      store_split4(a_hi, a_lo, kmajor_off(row, h0 + 4, kRows), v[4], v[5], v[6], v[7]);
+    }
     round(col0 + 128, w2_s, kH);                                             // dz2 -> columns [128, 256)
 
-    // ---- silu epilogue of layer 2: a2 -> operand planes, da2 kept in registers
-    float da2[kHh];
+    // ---- silu epilogue of layer 2: a2 -> operand planes, da2 parked over the dz2 columns just read
+    // (round 3 writes [0, 2 BO), round 4 [64, 64 + 2 BO): [128, 192) stays free until it is read back)
 #pragma unroll
     for (int cc = 0; cc < kHh; cc += 8) {
       const int c0 = half * kHh + cc;
@@ -225,23 +272,30 @@ __global__ void __launch_bounds__(kThreads, 1)
       tmem_ld8(tl + 128 + c0, dz);
       tmem_ld8(tl + 192 + c0, td);
       tmem_wait_ld();
-      float a[8];
+      float a[8], da[8];
 #pragma unroll
       for (int j = 0; j < 8; j++) {
         const float zz = (z[j] + ts[j]) + b2s[c0 + j];
         const float sg = sigmoid_f(zz);
         a[j] = zz * sg;
-        da2[cc + j] = sg * (1.f + zz * (1.f - sg)) * (dz[j] + td[j]);
+        da[j] = sg * (1.f + zz * (1.f - sg)) * (dz[j] + td[j]);
       }
 #pragma unroll
       for (int q = 0; q < 8; q += 4)
         store_split4(a_hi, a_lo, kmajor_off(row, c0 + q, kRows), a[q], a[q + 1], a[q + 2], a[q + 3]);
+      tmem_st8(tl + 128 + c0, da);
     }
+    tmem_wait_st();
     round(col0, w3_s, BO);                                                   // z3 -> columns [0, 2 BO)
 #pragma unroll
-    for (int hh = 0; hh < kHh; hh += 4)
-      store_split4(a_hi, a_lo, kmajor_off(row, half * kHh + hh, kRows), da2[hh], da2[hh + 1], da2[hh + 2],
-                   da2[hh + 3]);
+    for (int hh = 0; hh < kHh; hh += 8) {
+      float v[8];
+      tmem_ld8(park + hh, v);
+      tmem_wait_ld();
+      const int h0 = half * kHh + hh;
+      store_split4(a_hi, a_lo, kmajor_off(row, h0, kRows), v[0], v[1], v[2], v[3]);
+      store_split4(a_hi, a_lo, kmajor_off(row, h0 + 4, kRows), v[4], v[5], v[6], v[7]);
+    }
     round(col0 + 64, w3_s, BO);                                              // dz3 -> columns [64, 64 + 2 BO)
 
     // ---- output epilogue: 16-column groups split between the two halves (half 1 idle when BO = 16), read

@@ -209,6 +209,38 @@ def test_radial_fp64(small_graph, spline):
     assert rel(torch.autograd.grad((phi * G_).sum(), pos)[0], torch.autograd.grad((phi2 * G_).sum(), pos2)[0]) < 1e-10
 
 
+@pytest.mark.parametrize("B", [16, 6])
+def test_radial_spline_fp32(small_graph, B):
+    """fp32 compiled radial (B % 4 == 0 runs the 16-byte vector kernel, B = 6 the scalar one) against the fp64 torch
+    statement of the same fp32 tables: the bar is fp32 rounding of a cubic Hermite evaluation (rel 1e-5).  The tables
+    are smooth (sinusoids and their derivatives, like a compiled MLP): with random knot values the interpolant's slope
+    in grid units is O(1), so fp32 rounding of x = r/dr alone (ulp 6e-5 at x ~ 600) moves phi by ~1e-4."""
+    from face_b200.ops import EdgeVec, Radial
+    g = small_graph
+    torch.manual_seed(14)
+    n_el, G = 5, 1024
+    d32 = dict(dtype=torch.float32, device=DEV)
+    rg = torch.arange(G, dtype=torch.float64, device=DEV) * (5.0 / (G - 1))
+    amp, w, ph = (torch.randn(n_el * n_el, 1, B, dtype=torch.float64, device=DEV), 1 + 2 * torch.rand(1, 1, B, dtype=torch.float64, device=DEV),
+                  torch.rand(n_el * n_el, 1, B, dtype=torch.float64, device=DEV) * 6)
+    arg = w * rg[None, :, None] + ph
+    T, dT = (amp * torch.sin(arg)).to(**d32), (amp * w * torch.cos(arg)).to(**d32)
+    q = {"B": B, "n_el": n_el, "rc": 5.0, "spline": (T, dT, 5.0 / (G - 1))}
+    g32 = dict(g, shift=g["shift"].float())
+    pos = g["pos"].float().clone().requires_grad_(True)
+    phi = Radial.apply(EdgeVec.apply(pos, g32), g32, q)
+    assert phi.dtype == torch.float32 and phi.shape[1] == B
+    pos2 = g["pos"].float().double().clone().requires_grad_(True)
+    v2 = _torch_vec(g, pos2)
+    zp = g["zidx"][g["ei"].long()] * n_el + g["zidx"][g["ej"].long()]
+    phi2 = _radial_ref(q, v2.norm(dim=-1), zp, (T.double(), dT.double(), 5.0 / (G - 1)))
+    assert rel(phi.double(), phi2) < 1e-5
+    G_ = torch.randn_like(phi2)
+    d1 = torch.autograd.grad((phi.double() * G_).sum(), pos)[0].double()
+    d2 = torch.autograd.grad((phi2 * G_).sum(), pos2)[0]
+    assert rel(d1, d2) < 1e-4
+
+
 @pytest.mark.parametrize("dt", [torch.float64, torch.float32])
 @pytest.mark.parametrize("nc", [1, 10])
 def test_edge_msg_fp64(small_graph, nc, dt):

@@ -113,12 +113,16 @@ def test_radial_tc_rejects_unsupported_shapes():
 
 
 def test_radial_tc_many_tiles_persistent():
-    """3.1M edges: every 128-edge tile of the persistent grid is written (NaN-filled outputs beforehand)."""
+    """3.1M edges: every 128-edge tile of the persistent grid is written (NaN-filled outputs beforehand), to the
+    same fp64-anchored bar as the small cases."""
     n_el, nb, H, B = 5, 8, 64, 16
     vec, ei, ej, zidx = _edges(3_100_003, 5000, n_el, seed=11)
     W = _weights(n_el, nb, H, B, seed=12)
+    p64, d64 = _run("facek_radial_simt_fwd", vec, ei, ej, zidx, W, n_el, nb, H, B)
     p32, d32 = _run("facek_radial_simt_fwd", vec.float(), ei, ej, zidx, W, n_el, nb, H, B)
     ptc, dtc = _run("facek_radial_tc_fwd", vec.float(), ei, ej, zidx, W, n_el, nb, H, B)
     assert _status() == 0
     assert torch.isfinite(ptc).all() and torch.isfinite(dtc).all()
-    assert _rel(ptc, p32.double()) < 4e-6 and _rel(dtc, d32.double()) < 4e-6
+    for tc, s32, ref in ((ptc, p32, p64), (dtc, d32, d64)):
+        e_tc, e_32 = _rel(tc, ref), _rel(s32, ref)
+        assert e_tc < max(4 * e_32, 2e-6), (e_tc, e_32)
