@@ -831,8 +831,8 @@ def channel_moments(q, gr, geo, h, A_sets, eq, phi):
     base = F.linear(h, q["msg_w"], q["msg_b"]) if cp else h                        # (N, C)
     Gt = tsrc = None
     if q["directional"]:
-        src1 = eq[0] if q["eq_in"] else torch.cat([A[1] for A in A_sets], 2)        # (3, N, cprev)
-        src2 = eq[1] if q["eq_in"] else torch.cat([A[2] for A in A_sets], 2)        # (6, N, cprev)
+        src1 = eq[0] if q["eq_in"] else _cat([A[1] for A in A_sets], 2)        # (3, N, cprev)
+        src2 = eq[1] if q["eq_in"] else _cat([A[2] for A in A_sets], 2)        # (6, N, cprev)
         Vb = src1 @ q["pvtT"]
         Mb = src2 @ q["pmtT"]
         Vd, Md = Vb[..., :Kd], Mb[..., :Kd]
@@ -863,6 +863,11 @@ def channel_moments(q, gr, geo, h, A_sets, eq, phi):
     return A
 
 
+def _cat(ts, dim):
+    """torch.cat, without the copy when there is one tensor."""
+    return ts[0] if len(ts) == 1 else torch.cat(ts, dim)
+
+
 def block_forward(P, t, gr, geo, h, A_sets, eq):
     """One interaction pass (face/model.py:310-339 with FactorBlock.moments :460-534, or the CP form and the
     non-factorised MomentBlock.moments :160-201)."""
@@ -871,7 +876,10 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
     C, B, K, Kd = q["C"], q["B"], q["K"], q["Kd"]
     vec, Y = geo["vec"], geo["Y"]
     phi = Radial.apply(vec, gr, q)                                                   # (E, B), env included
-    s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1).contiguous()   # (4, N, C)
+    s = geo["consts"].get(("scale", t))
+    if s is None:                                # elem_scale[Z] / avg_nb as (4, N, C): fixed by graph and weights
+        s = (q["elem_scale"][geo["zidx"]] / geo["avg_nb"]).view(N, 4, C).transpose(0, 1).contiguous()
+        geo["consts"][("scale", t)] = s
     if q["form"] != "factor":
         A = channel_moments(q, gr, geo, h, A_sets, eq, phi)
         A = [BcastMul.apply(A[l], s[l]) for l in range(4)]
@@ -879,8 +887,8 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
     msgtab = linear(h, (q["msg_w"], q["msg_b"]), q["msgD"])                          # (N, K)
     Gt = None
     if q["directional"]:
-        src1 = eq[0] if q["eq_in"] else torch.cat([A[1] for A in A_sets], 2)        # (3, N, cprev)
-        src2 = eq[1] if q["eq_in"] else torch.cat([A[2] for A in A_sets], 2)        # (6, N, cprev)
+        src1 = eq[0] if q["eq_in"] else _cat([A[1] for A in A_sets], 2)        # (3, N, cprev)
+        src2 = eq[1] if q["eq_in"] else _cat([A[2] for A in A_sets], 2)        # (6, N, cprev)
         Vb = mm(src1, q["pvtT"], q["pvtD"])                                           # (3, N, nt*Kd)
         Mb = mm(src2, q["pmtT"], q["pmtD"])                                           # (6, N, nt*Kd)
         Vd, Md = Vb[..., :Kd], Mb[..., :Kd]
@@ -906,7 +914,7 @@ def _invariants_readout(P, q, h, A_sets, A, N):
     """Invariants, norm, readout and gated equivariant outputs of a pass (face/model.py:204-339)."""
     # invariants (face/model.py:204-270): projections straight into the node kernel's layout
     sets = A_sets + [A]
-    ys = [mm(torch.cat([a[l] for a in sets], 2), q["projT"][l], q["projD"][l]) for l in range(4)]   # (k_l, N, 3C)
+    ys = [mm(_cat([a[l] for a in sets], 2), q["projT"][l], q["projD"][l]) for l in range(4)]   # (k_l, N, 3C)
     a_w = q["vpath"] if q["eq_out"] else None
     b_w = q["mpath"] if q["eq_out"] else None
     inv, V, Ms = NodeAlgebraEngine.apply(*ys, a_w, b_w, q["eq_out"], P["max_body"])
@@ -1004,6 +1012,18 @@ def coulomb_term(P, gr, geo, h, pos):
     return chi * q + 0.5 * J * q * q + per_atom(e_es / natoms.to(q.dtype), batch, nstr), q
 
 
+def _graph_consts(P, Z):
+    """Per-graph constants of an evaluation: element indices (int64 and int32) and, filled in by the passes, the
+    per-atom element scalings.  They depend only on the atomic numbers and the prepared weights, so they are kept
+    for the most recent Z tensor (same object, unmodified) and rebuilt when the graph changes."""
+    c = P.get("_graph_consts")
+    if c is None or c[0] is not Z or c[1] != Z._version:
+        zidx = P["zmap"][Z]
+        c = (Z, Z._version, zidx, zidx.to(torch.int32).contiguous(), {})
+        P["_graph_consts"] = c
+    return c[2], c[3], c[4]
+
+
 def local_energies(model, gr, pos, between=None):
     """Per-atom model energies (without physics terms) and final features h for positions `pos` (any
     differentiable tensor) on graph `gr` (face/model.py:665-686).
@@ -1014,11 +1034,11 @@ def local_energies(model, gr, pos, between=None):
     dtype = model.embed.weight.dtype
     P = prepare(model, dtype, pos.device)
     P["max_body"] = model.max_body
-    zidx = P["zmap"][gr["Z"]]
-    gr = dict(gr, zidx=zidx.to(torch.int32).contiguous())
+    zidx, zidx32, consts = _graph_consts(P, gr["Z"])
+    gr = dict(gr, zidx=zidx32)
     vec = EdgeVec.apply(pos, gr)
     Y = EdgeSym.apply(vec)
-    geo = {"vec": vec, "Y": Y, "zidx": zidx, "avg_nb": P["avg_nb"]}
+    geo = {"vec": vec, "Y": Y, "zidx": zidx, "avg_nb": P["avg_nb"], "consts": consts}
     h = P["embed"][zidx]
     e_at = P["E0"][zidx]
     A_sets, eq = [], None
