@@ -3,6 +3,11 @@
 //
 //   C[M, N] (= or +=) A[M, K] . W[K, N] (+ bias[N])
 //
+// A and C may each come as two column blocks (facek_gemm_tc_split): A = [A1 | A2] split at a multiple of 32 columns
+// (the A producer takes each 32-wide K chunk from one of two tensor maps) and C = [C1 | C2] split at a multiple of 32
+// (each 32-column store block goes to one of two outputs), so a layer on concatenated features reads its inputs
+// where they are and its adjoint writes the two input gradients as separate tensors, with no concatenation copy.
+//
 // fp32 accuracy on the tf32 datapath through the 3-term split (tc.cuh). W is constant during a step, so it is
 // packed once (facek_gemm_pack) into an "image": for every N tile (Nt columns) and every 32-wide K chunk, a tf32
 // hi plane and a lo plane in the K-major no-swizzle operand layout.
@@ -64,6 +69,10 @@ struct GemmArgs {
   int64_t ldc;
   int beta;                   // 1: C += A.W
   uint32_t tmem_cols;
+  int k1_chunks;              // K chunks read from the first A map; the rest from the second (= k_chunks: one map)
+  int64_t n1;                 // output columns [0, n1) to C / cmap, [n1, N) to C2 / cmap2 (= N: one output)
+  float* C2;
+  int64_t ldc2;
 };
 
 // Shared memory per N tile (H16 = Nt / 32): a deep ring of SA A tiles (the only HBM stream), a shallow ring of SW
@@ -152,7 +161,9 @@ __device__ __forceinline__ void mbar_arrive(uint64_t* mbar) {
 
 template <int H16>
 __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUtensorMap amap,
-                                                     const __grid_constant__ CUtensorMap cmap, GemmArgs g) {
+                                                     const __grid_constant__ CUtensorMap amap2,
+                                                     const __grid_constant__ CUtensorMap cmap,
+                                                     const __grid_constant__ CUtensorMap cmap2, GemmArgs g) {
   constexpr int SA = Ring<H16>::SA, SW = Ring<H16>::SW;
   constexpr int Nt = 32 * H16;
   constexpr int HALF = Nt / 2;                                 // columns per compute warpgroup
@@ -209,13 +220,19 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUt
     if (warp == 8 && lane == 0) {
       // ---------------------------------------------------------------- A producer (TMA, deep ring)
       asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&amap)) : "memory");
+      if (g.k1_chunks < g.k_chunks)
+        asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(&amap2)) : "memory");
       Cursor pc;
       pc.start(blockIdx.x, g.n_tiles);
       for (int64_t j = 0; j < total; j++) {
         const int s = (int)(j % SA);
         if (j >= SA && !mbar_wait(&emptyA[s], (uint32_t)(((j / SA) - 1) & 1), ab)) break;
         mbar_expect_tx(&fullA[s], kPlane);
-        tma_load_2d(aring + (uint32_t)s * kPlane, &amap, pc.kc * kKc, (int)(pc.mt * kM), &fullA[s]);
+        if (pc.kc < g.k1_chunks)      // A = [A1 | A2] split at a 32-column chunk (k1_chunks = k_chunks: no A2)
+          tma_load_2d(aring + (uint32_t)s * kPlane, &amap, pc.kc * kKc, (int)(pc.mt * kM), &fullA[s]);
+        else
+          tma_load_2d(aring + (uint32_t)s * kPlane, &amap2, (pc.kc - g.k1_chunks) * kKc, (int)(pc.mt * kM),
+                      &fullA[s]);
         pc.next(g.k_chunks, g.n_tiles, gridDim.x);
       }
     } else if (warp == 9 && lane == 0) {
@@ -312,8 +329,13 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUt
             fence_proxy_async_smem();                            // staging writes -> async proxy
             bar_sync(1 + wg, kM);
             if (row == 0) {
-              if (g.beta) tma_add_2d(&cmap, (int)gc0, (int)row0, sb);
-              else tma_store_2d(&cmap, (int)gc0, (int)row0, sb);
+              // C = [C1 | C2] split at a 32-column block; without C2 every block, including those past N that
+              // the copy engine clips, goes to the first map (the second one is empty then)
+              const bool second = g.C2 != nullptr && gc0 >= g.n1;
+              const CUtensorMap* cm = second ? &cmap2 : &cmap;
+              const int x = (int)(second ? gc0 - g.n1 : gc0);
+              if (g.beta) tma_add_2d(cm, x, (int)row0, sb);
+              else tma_store_2d(cm, x, (int)row0, sb);
               bulk_commit();
             }
           }
@@ -340,7 +362,7 @@ __global__ void __launch_bounds__(kThr, 1) gemm_tc_k(const __grid_constant__ CUt
                 o.z += g.bias[gc + 2];
                 o.w += g.bias[gc + 3];
               }
-              float* out = g.C + grow * g.ldc + gc;
+              float* out = (g.C2 == nullptr || gc < g.n1) ? g.C + grow * g.ldc + gc : g.C2 + grow * g.ldc2 + (gc - g.n1);
               if (g.beta) {
                 const float4 p = *reinterpret_cast<const float4*>(out);
                 o.x += p.x;
@@ -441,7 +463,8 @@ EncodeTiledFn encode_fn() {
 }
 
 template <int H16>
-int launch_gemm(const CUtensorMap& amap, const CUtensorMap& cmap, const GemmArgs& g, void* stream) {
+int launch_gemm(const CUtensorMap& amap, const CUtensorMap& amap2, const CUtensorMap& cmap, const CUtensorMap& cmap2,
+                const GemmArgs& g, void* stream) {
   constexpr int Nt = 32 * H16;
   constexpr int SA = Ring<H16>::SA, SW = Ring<H16>::SW;
   const size_t smem =
@@ -450,7 +473,7 @@ int launch_gemm(const CUtensorMap& amap, const CUtensorMap& cmap, const GemmArgs
   cudaFuncSetAttribute(gemm_tc_k<H16>, cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem);
   const int64_t units = ((g.M + kM - 1) / kM) * g.n_tiles;
   const int grid = (int)std::min<int64_t>(units, sm_count());
-  gemm_tc_k<H16><<<grid, kThr, smem, as_stream(stream)>>>(amap, cmap, g);
+  gemm_tc_k<H16><<<grid, kThr, smem, as_stream(stream)>>>(amap, amap2, cmap, cmap2, g);
   return launch_status("facek_gemm_tc");
 }
 
@@ -488,29 +511,62 @@ extern "C" int facek_gemm_pack(const float* W, int64_t K, int64_t N, int64_t str
   return launch_status("facek_gemm_pack");
 }
 
-extern "C" int facek_gemm_tc(const float* A, int64_t M, int64_t K, int64_t lda, const float* image, int64_t N,
-                             const float* bias, float* C, int64_t ldc, int32_t beta, void* stream) {
+namespace {
+
+// A 2D fp32 tensor map with 128-byte swizzle: rows x cols (row stride ld floats), box 32 columns x 128 rows
+int encode_2d(EncodeTiledFn enc, CUtensorMap* map, const float* base, int64_t rows, int64_t cols, int64_t ld,
+              CUtensorMapL2promotion promo, const char* what) {
+  const cuuint64_t dims[2] = {(cuuint64_t)cols, (cuuint64_t)rows};
+  const cuuint64_t strides[1] = {(cuuint64_t)ld * 4};
+  const cuuint32_t box[2] = {(cuuint32_t)kKc, (cuuint32_t)kM};
+  const cuuint32_t estr[2] = {1, 1};
+  const CUresult cr = enc(map, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, promo,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  FACEK_CHECK_ARG(cr == CUDA_SUCCESS, "facek_gemm_tc: %s tensor map encoding failed (%d)", what, (int)cr);
+  return FACEK_OK;
+}
+
+bool operand_ok(const float* p, int64_t cols, int64_t ld) {
+  return p && cols > 0 && cols % 4 == 0 && ld % 4 == 0 && ld >= cols && (reinterpret_cast<uintptr_t>(p) & 15) == 0;
+}
+
+// [C1 | C2] (=|+)= [A1 | A2] . W (+ bias): A1 holds K columns 0 .. K1-1 and A2 the rest (A2 null: K1 = K), C1 the
+// output columns 0 .. N1-1 and C2 the rest (C2 null: N1 = N)
+int gemm_run(const float* A1, int64_t lda1, int64_t K1, const float* A2, int64_t lda2, int64_t M, int64_t K,
+             const float* image, int64_t N, const float* bias, float* C1, int64_t ldc1, int64_t N1, float* C2,
+             int64_t ldc2, int beta, void* stream) {
   FACEK_CHECK_ARG(M >= 0 && K > 0 && N > 0, "facek_gemm_tc: bad sizes M=%lld K=%lld N=%lld", (long long)M,
                   (long long)K, (long long)N);
   if (M == 0) return FACEK_OK;
-  FACEK_CHECK_ARG(A && image && C, "facek_gemm_tc: null tensor");
-  FACEK_CHECK_ARG(K % 4 == 0 && lda % 4 == 0 && lda >= K && (reinterpret_cast<uintptr_t>(A) & 15) == 0,
+  FACEK_CHECK_ARG(image && (reinterpret_cast<uintptr_t>(image) & 15) == 0,
+                  "facek_gemm_tc: image null or not 16-byte aligned");
+  FACEK_CHECK_ARG(operand_ok(A1, K1, lda1),
                   "facek_gemm_tc: A needs K %% 4 == 0, lda %% 4 == 0, lda >= K and 16-byte alignment");
-  FACEK_CHECK_ARG(N % 4 == 0 && ldc % 4 == 0 && ldc >= N && (reinterpret_cast<uintptr_t>(C) & 15) == 0,
+  FACEK_CHECK_ARG(operand_ok(C1, N1, ldc1),
                   "facek_gemm_tc: C needs N %% 4 == 0, ldc %% 4 == 0, ldc >= N and 16-byte alignment");
-  FACEK_CHECK_ARG((reinterpret_cast<uintptr_t>(image) & 15) == 0, "facek_gemm_tc: image not 16-byte aligned");
+  if (A2) {
+    FACEK_CHECK_ARG(K1 % kKc == 0 && K1 < K && operand_ok(A2, K - K1, lda2),
+                    "facek_gemm_tc_split: A1 needs K1 %% 32 == 0, K1 < K; A2 as A (K - K1 columns)");
+  } else {
+    FACEK_CHECK_ARG(K1 == K, "facek_gemm_tc_split: without A2, K1 must equal K");
+  }
+  if (C2) {
+    FACEK_CHECK_ARG(N1 % 32 == 0 && N1 < N && operand_ok(C2, N - N1, ldc2),
+                    "facek_gemm_tc_split: C1 needs N1 %% 32 == 0, N1 < N; C2 as C (N - N1 columns)");
+  } else {
+    FACEK_CHECK_ARG(N1 == N, "facek_gemm_tc_split: without C2, N1 must equal N");
+  }
   FACEK_CHECK_ARG(M < (int64_t)1 << 31 && K < (int64_t)1 << 31, "facek_gemm_tc: M, K must be < 2^31");
   EncodeTiledFn enc = encode_fn();
   FACEK_CHECK_ARG(enc != nullptr, "facek_gemm_tc: cuTensorMapEncodeTiled unavailable");
-  CUtensorMap amap;
-  const cuuint64_t dims[2] = {(cuuint64_t)K, (cuuint64_t)M};
-  const cuuint64_t strides[1] = {(cuuint64_t)lda * 4};
-  const cuuint32_t box[2] = {(cuuint32_t)kKc, (cuuint32_t)kM};
-  const cuuint32_t estr[2] = {1, 1};
-  const CUresult cr = enc(&amap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, const_cast<float*>(A), dims, strides, box, estr,
-                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
-                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-  FACEK_CHECK_ARG(cr == CUDA_SUCCESS, "facek_gemm_tc: tensor map encoding failed (%d)", (int)cr);
+  CUtensorMap amap, amap2;
+  std::memset(&amap2, 0, sizeof(amap2));
+  int st = encode_2d(enc, &amap, A1, M, K1, lda1, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "input");
+  if (st != FACEK_OK) return st;
+  if (A2 && (st = encode_2d(enc, &amap2, A2, M, K - K1, lda2, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, "second input")) !=
+                FACEK_OK)
+    return st;
   GemmArgs g{};
   g.M = M;
   g.K = K;
@@ -519,30 +575,45 @@ extern "C" int facek_gemm_tc(const float* A, int64_t M, int64_t K, int64_t lda, 
   g.Nt = pick_nt(N);
   g.n_tiles = (int)((N + g.Nt - 1) / g.Nt);
   g.k_chunks = (int)((K + kKc - 1) / kKc);
+  g.k1_chunks = A2 ? (int)(K1 / kKc) : g.k_chunks;
   g.bias = bias;
-  g.C = C;
-  g.ldc = ldc;
+  g.C = C1;
+  g.ldc = ldc1;
+  g.n1 = N1;
+  g.C2 = C2;
+  g.ldc2 = ldc2;
   g.beta = beta ? 1 : 0;
   uint32_t cols = 32;
   while (cols < (uint32_t)(kNB * g.Nt)) cols <<= 1;             // kNB chunk partials
   g.tmem_cols = cols;
   // C as a TMA destination for the 64- and 128-column tiles (box 32 columns x 128 rows, 128-byte swizzle; TMA
   // clips the rows >= M and columns >= N of the last tiles); unused by the other widths
-  CUtensorMap cmap;
+  CUtensorMap cmap, cmap2;
   std::memset(&cmap, 0, sizeof(cmap));
+  std::memset(&cmap2, 0, sizeof(cmap2));
   if (g.Nt % 64 == 0) {
-    const cuuint64_t cdims[2] = {(cuuint64_t)N, (cuuint64_t)M};
-    const cuuint64_t cstrides[1] = {(cuuint64_t)ldc * 4};
-    const cuuint32_t cbox[2] = {32, (cuuint32_t)kM};
-    const CUresult cc = enc(&cmap, CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 2, C, cdims, cstrides, cbox, estr,
-                            CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                            CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
-    FACEK_CHECK_ARG(cc == CUDA_SUCCESS, "facek_gemm_tc: output tensor map encoding failed (%d)", (int)cc);
+    if ((st = encode_2d(enc, &cmap, C1, M, N1, ldc1, CU_TENSOR_MAP_L2_PROMOTION_NONE, "output")) != FACEK_OK) return st;
+    if (C2 && (st = encode_2d(enc, &cmap2, C2, M, N - N1, ldc2, CU_TENSOR_MAP_L2_PROMOTION_NONE, "second output")) !=
+                  FACEK_OK)
+      return st;
   }
   switch (g.Nt / 32) {
-    case 1: return launch_gemm<1>(amap, cmap, g, stream);
-    case 2: return launch_gemm<2>(amap, cmap, g, stream);
-    case 3: return launch_gemm<3>(amap, cmap, g, stream);
-    default: return launch_gemm<4>(amap, cmap, g, stream);
+    case 1: return launch_gemm<1>(amap, amap2, cmap, cmap2, g, stream);
+    case 2: return launch_gemm<2>(amap, amap2, cmap, cmap2, g, stream);
+    case 3: return launch_gemm<3>(amap, amap2, cmap, cmap2, g, stream);
+    default: return launch_gemm<4>(amap, amap2, cmap, cmap2, g, stream);
   }
+}
+
+}  // namespace
+
+extern "C" int facek_gemm_tc(const float* A, int64_t M, int64_t K, int64_t lda, const float* image, int64_t N,
+                             const float* bias, float* C, int64_t ldc, int32_t beta, void* stream) {
+  return gemm_run(A, lda, K, nullptr, 0, M, K, image, N, bias, C, ldc, N, nullptr, 0, beta, stream);
+}
+
+extern "C" int facek_gemm_tc_split(const float* A1, int64_t lda1, int64_t K1, const float* A2, int64_t lda2,
+                                   int64_t M, int64_t K, const float* image, int64_t N, const float* bias, float* C1,
+                                   int64_t ldc1, int64_t N1, float* C2, int64_t ldc2, int32_t beta, void* stream) {
+  return gemm_run(A1, lda1, K1, A2, lda2, M, K, image, N, bias, C1, ldc1, N1, C2, ldc2, beta, stream);
 }

@@ -52,6 +52,7 @@ SIGNATURES = {
     "facek_gemm_image_floats": [I64, I64],
     "facek_gemm_pack": [P, I64, I64, I64, I64, P, P],
     "facek_gemm_tc": [P, I64, I64, I64, P, I64, P, P, I64, I32, P],
+    "facek_gemm_tc_split": [P, I64, I64, P, I64, I64, I64, P, I64, P, P, I64, I64, P, I64, I32, P],
     "facek_radial_spline_fwd": [I32, P, P, P, P, I32, D, I32, D, I32, P, P, P, P, I64, P],
     "facek_radial_bwd": [I32, P, P, P, I32, P, I32, I64, P],
     "facek_edge_msg_fwd": [I32, P, P, P, P, P, I32, I32, P, I64, I64, P],

@@ -664,6 +664,43 @@ class TCMatmul(torch.autograd.Function):
         return dx1.view(*ctx.lead, d1.K), None, dx2, None
 
 
+class TCMatmulCat(torch.autograd.Function):
+    """y = [x1 | x2] @ W on the tensor cores without the concatenation in memory (facek_gemm_tc_split): the GEMM
+    takes each 32-wide K chunk from x1 or x2 where they lie, and the adjoint writes dx1 and dx2 as two tensors, so
+    neither the forward's concatenation nor the adjoint's slice copies exist.  x1 (..., K1) with K1 a multiple of
+    32, x2 (..., K - K1), D packed for the full (K, N) weight; weights constant."""
+
+    @staticmethod
+    def forward(ctx, x1, x2, d):
+        lead, K1 = x1.shape[:-1], x1.shape[-1]
+        a1, a2 = _rows(x1, K1), _rows(x2, d.K - K1)
+        M = a1.shape[0]
+        y = torch.empty(M, d.N, dtype=x1.dtype, device=x1.device)
+        _lib.call("facek_gemm_tc_split", _p(a1), a1.stride(0), K1, _p(a2), a2.stride(0), M, d.K, _p(d.img), d.N,
+                  _p(d.b), _p(y), y.stride(0), d.N, None, 0, 0, _lib.stream())
+        ctx.d, ctx.K1, ctx.lead = d, K1, lead
+        return y.view(*lead, d.N)
+
+    @staticmethod
+    def backward(ctx, dy):
+        d, K1 = ctx.d, ctx.K1
+        g = _rows(dy, d.N)
+        M = g.shape[0]
+        dx1 = torch.empty(M, K1, dtype=dy.dtype, device=dy.device)
+        dx2 = torch.empty(M, d.K - K1, dtype=dy.dtype, device=dy.device)
+        _lib.call("facek_gemm_tc_split", _p(g), g.stride(0), d.N, None, 0, M, d.N, _p(d.imgT), d.K, None, _p(dx1),
+                  dx1.stride(0), K1, _p(dx2), dx2.stride(0), 0, _lib.stream())
+        return dx1.view(*ctx.lead, K1), dx2.view(*ctx.lead, d.K - K1), None
+
+
+def mm_cat(xs, W, D=None):
+    """torch.cat(xs, -1) @ W; two fp32 inputs whose first width is a multiple of 32 take the split GEMM."""
+    if (D is not None and len(xs) == 2 and xs[0].dtype == torch.float32 and xs[0].shape[-1] % 32 == 0
+            and xs[1].shape[-1] % 4 == 0):
+        return TCMatmulCat.apply(xs[0], xs[1], D)
+    return mm(_cat(xs, -1), W, D)
+
+
 def mm(x, W, D=None, x2=None, W2=None, D2=None):
     """x @ W (+ x2 @ W2): the tensor-core GEMM when packed weights D are given (fp32), else torch."""
     if D is not None and x.dtype == torch.float32 and (x2 is None or D2 is not None):
@@ -914,7 +951,7 @@ def _invariants_readout(P, q, h, A_sets, A, N):
     """Invariants, norm, readout and gated equivariant outputs of a pass (face/model.py:204-339)."""
     # invariants (face/model.py:204-270): projections straight into the node kernel's layout
     sets = A_sets + [A]
-    ys = [mm(_cat([a[l] for a in sets], 2), q["projT"][l], q["projD"][l]) for l in range(4)]   # (k_l, N, 3C)
+    ys = [mm_cat([a[l] for a in sets], q["projT"][l], q["projD"][l]) for l in range(4)]         # (k_l, N, 3C)
     a_w = q["vpath"] if q["eq_out"] else None
     b_w = q["mpath"] if q["eq_out"] else None
     inv, V, Ms = NodeAlgebraEngine.apply(*ys, a_w, b_w, q["eq_out"], P["max_body"])

@@ -205,6 +205,15 @@ int facek_gemm_pack(const float* W, int64_t K, int64_t N, int64_t stride_k, int6
                     void* stream);
 int facek_gemm_tc(const float* A, int64_t M, int64_t K, int64_t lda, const float* image, int64_t N,
                   const float* bias, float* C, int64_t ldc, int32_t beta, void* stream);
+/* The same GEMM on a concatenated input and/or into a split output, without the concatenation in memory (the
+ * reference concatenates the passes' moment sets with torch.cat before each projection, face/model.py:209):
+ *   [C1 | C2] (beta ? += : =) [A1 | A2] . W (+ bias).
+ * A1 is M x K1 (lda1), A2 is M x (K - K1) (lda2), K1 a multiple of 32; A2 = NULL means K1 = K. C1 is M x N1 (ldc1),
+ * C2 is M x (N - N1) (ldc2), N1 a multiple of 32; C2 = NULL means N1 = N. Each block follows facek_gemm_tc's rules
+ * on widths, strides and alignment. The image is the one packed for the full K x N. */
+int facek_gemm_tc_split(const float* A1, int64_t lda1, int64_t K1, const float* A2, int64_t lda2, int64_t M,
+                        int64_t K, const float* image, int64_t N, const float* bias, float* C1, int64_t ldc1,
+                        int64_t N1, float* C2, int64_t ldc2, int32_t beta, void* stream);
 /* Status of the tensor-core kernels (no reference counterpart): bit 0 set when a kernel gave up waiting for its
  * MMAs (bounded wait) and returned early with its outputs incomplete. Synchronises the device; clear != 0 resets. */
 int facek_tc_status(int32_t* status, int32_t clear);
