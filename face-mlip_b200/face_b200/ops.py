@@ -810,6 +810,9 @@ def prepare(model, dtype, dev):
                 w = _lin(model, getattr(blk, name), dtype, dev)[0]                           # (C, B*2*Kd) cols (b,t,kd)
                 q[name + "T"] = w.view(C, B, 2, Kd).permute(0, 2, 1, 3).reshape(C, 2 * B * Kd).t().contiguous()
                 q[name + "D"] = pk(q[name + "T"])
+            # channel map and transport map of ranks 1, 2 as one layer on [D_l | T_l] (facek_gemm_tc_split)
+            q["mixtT"] = {l: torch.cat([q["mixT"][l], q["tmix%dT" % l]], 0) for l in (1, 2)}
+            q["mixtD"] = {l: pk(q["mixtT"][l]) for l in (1, 2)}
         blocks.append(q)
     P["blocks"] = blocks
     P["terms"] = list(model.terms.keys())
@@ -891,13 +894,22 @@ def channel_moments(q, gr, geo, h, A_sets, eq, phi):
         if Gt is not None:
             T1, T2 = Transport.apply(phi[:, :B].contiguous(), vec, Gt, gr)
             tpl = {1: (T1, q["tmix1T"], q["tmix1D"]), 2: (T2, q["tmix2T"], q["tmix2D"])}
-        return [mm(D[l], q["mixT"][l], q["mixD"][l], *tpl.get(l, (None, None, None))) for l in range(4)]
+        return [_mix(q, l, D[l], tpl) for l in range(4)]
     A = list(D)
     if tsrc is not None:
         A1, A2 = moment_transport(phi, Y, tsrc[0], tsrc[1], gr, C)
         A[1] = A[1] + A1
         A[2] = A[2] + A2
     return A
+
+
+def _mix(q, l, Dl, tpl):
+    """Channel map of rank l, plus the transport map where the pass has one: one GEMM on [D_l | T_l] when the
+    stacked weight is packed, else D_l @ mix (+ T_l @ tmix)."""
+    t = tpl.get(l)
+    if t is not None and q.get("mixtD", {}).get(l) is not None:
+        return mm_cat([Dl, t[0]], q["mixtT"][l], q["mixtD"][l])
+    return mm(Dl, q["mixT"][l], q["mixD"][l], *(t or (None, None, None)))
 
 
 def _cat(ts, dim):
@@ -942,7 +954,7 @@ def block_forward(P, t, gr, geo, h, A_sets, eq):
     if Gt is not None:
         T1, T2 = Transport.apply(phi, vec, Gt, gr)                                   # (3|6, N, 2*B*Kd)
         tpl = {1: (T1, q["tmix1T"], q["tmix1D"]), 2: (T2, q["tmix2T"], q["tmix2D"])}
-    A = [mm(D[l], q["mixT"][l], q["mixD"][l], *tpl.get(l, (None, None, None))) for l in range(4)]   # (k_l, N, C)
+    A = [_mix(q, l, D[l], tpl) for l in range(4)]                                    # (k_l, N, C)
     A = [BcastMul.apply(A[l], s[l]) for l in range(4)]
     return _invariants_readout(P, q, h, A_sets, A, N)
 

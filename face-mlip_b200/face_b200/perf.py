@@ -9,7 +9,7 @@ Per launch, the ALGORITHMIC bytes (each input read once, each output written onc
                                                      dY out) + 2*e*nc*N*K (message tables) + 4(N+1) + 8E (rows, ei, ej)
                                               flops  2*E*(40*B*K + 40*B + 2*nc*K)
   channel GEMM      facek_gemm_tc             bytes  4*rows*(K + N*(1+beta)) + 8*K*N (split weight image)
-                                              flops  2*rows*K*N
+                    facek_gemm_tc_split       flops  2*rows*K*N  (both entries, one row)
 
 (e = element size, E edges, N atoms; the tensor-core density adjoint facek_density_msg_tc_xm_bwd has the same
 algorithmic bytes and FLOPs as the CUDA-core one.)  Each kernel is reported against the measured HBM copy bandwidth and against
@@ -26,10 +26,15 @@ from . import _lib
 SMS, FP32_LANES = 148, 128
 
 ENTRIES = {"dens_bwd": "facek_density_msg_xm_bwd", "dens_bwd_tc": "facek_density_msg_tc_xm_bwd",
-           "gemm": "facek_gemm_tc", "dens_fwd": "facek_density_xm_fwd"}
+           "gemm": ("facek_gemm_tc", "facek_gemm_tc_split"), "dens_fwd": "facek_density_xm_fwd"}
 KERNEL_NAMES = {"dens_bwd": "dens_bwd_lane_k (facek_density_msg_xm_bwd)",
                 "dens_bwd_tc": "dens_bwd_tc_k + message dY (facek_density_msg_tc_xm_bwd)",
-                "gemm": "gemm_tc_k (facek_gemm_tc)", "dens_fwd": "dens_fwd_k (facek_density_xm_fwd)"}
+                "gemm": "gemm_tc_k (facek_gemm_tc, facek_gemm_tc_split)",
+                "dens_fwd": "dens_fwd_k (facek_density_xm_fwd)"}
+
+
+def _names(v):
+    return v if isinstance(v, tuple) else (v,)
 
 
 def peaks(root):
@@ -45,9 +50,10 @@ def peaks(root):
 
 def start():
     """Record events and arguments of the dominant entry points from now on."""
-    for name in ENTRIES.values():
-        _lib.TIMED[name] = []
-        _lib.ARGS[name] = []
+    for names in ENTRIES.values():
+        for name in _names(names):
+            _lib.TIMED[name] = []
+            _lib.ARGS[name] = []
 
 
 def _sizes(name, args, E, N, B, K, esz):
@@ -60,6 +66,9 @@ def _sizes(name, args, E, N, B, K, esz):
     if name == "facek_gemm_tc":
         rows, k, n, beta = int(args[1]), int(args[2]), int(args[5]), int(args[9])
         return 4 * rows * (k + n * (1 + beta)) + 8 * k * n, 2.0 * rows * k * n
+    if name == "facek_gemm_tc_split":
+        rows, k, n, beta = int(args[5]), int(args[6]), int(args[8]), int(args[15])
+        return 4 * rows * (k + n * (1 + beta)) + 8 * k * n, 2.0 * rows * k * n
     raise KeyError(name)
 
 
@@ -68,13 +77,17 @@ def collect(E, N, B, K, esz, steps, root, traffic=None):
     `traffic` maps a kernel key to measured DRAM bytes per launch (ncu), when known."""
     pk = peaks(root)
     rows = []
-    for key, name in ENTRIES.items():
-        ev = _lib.TIMED.pop(name, None) or []
-        args = _lib.ARGS.pop(name, None) or []
+    for key, names in ENTRIES.items():
+        ev, sz = [], []
+        for name in _names(names):
+            e_n = _lib.TIMED.pop(name, None) or []
+            a_n = _lib.ARGS.pop(name, None) or []
+            ev += e_n
+            sz += [_sizes(name, a, E, N, B, K, esz) for a in a_n]
         if not ev:
             continue
         ts = [s.elapsed_time(t) / 1e3 for s, t in ev]
-        by, fl = zip(*[_sizes(name, a, E, N, B, K, esz) for a in args])
+        by, fl = zip(*sz)
         t_tot, b_tot, f_tot = sum(ts), sum(by), sum(fl)
         launches = len(ts)
         gbs = b_tot / t_tot / 1e9
