@@ -114,7 +114,7 @@ class FACECalculator(Calculator):
                 return dict(g, pos=p64.to(self.dtype))
         rc_long = self.model.terms["disp"].r_long if "disp" in self.model.terms else None
         self._graph = build_graph([at], self.model.rc, device=self.device, dtype=self.dtype, skin=self.skin,
-                                  rc_long=rc_long)
+                                  rc_long=rc_long, pos64=self._positions(pos))
         self._key = key
         self.rebuilds += 1
         return self._graph

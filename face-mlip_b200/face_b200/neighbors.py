@@ -96,23 +96,25 @@ def structure_meta(sizes, cells, device):
 LR_KEYS = ("row_ptr", "ei", "ej", "S", "shift", "rev")
 
 
-def build_graph(structures, rc, device="cuda", dtype=torch.float32, skin=0.0, rc_long=None):
+def build_graph(structures, rc, device="cuda", dtype=torch.float32, skin=0.0, rc_long=None, pos64=None):
     """CSR neighbour graph of a batch of structures, built on the GPU (see module docstring).  With skin > 0 the
     list holds every pair closer than rc + skin (for reuse across MD steps; "coul_cut" = rc keeps the Coulomb
     real-space sum on the pairs closer than rc, and the model's envelope is zero beyond rc).  rc_long adds the
-    long-range pair list of the dispersion term under "lr" (face/datasets.py:53-55, GraphSet(rc_long=...))."""
-    g = _build_graph(structures, rc + skin, device, dtype)
+    long-range pair list of the dispersion term under "lr" (face/datasets.py:53-55, GraphSet(rc_long=...)).
+    pos64, when given, is the batch's positions already on the device (float64, (N, 3), e.g. uploaded from pinned
+    memory by the caller) and replaces the upload from the structures."""
+    g = _build_graph(structures, rc + skin, device, dtype, pos64)
     if skin > 0:
         g["coul_cut"] = float(rc)
         g["rc"] = float(rc)
         g["skin"] = float(skin)
     if rc_long:
-        lr = _build_graph(structures, rc_long + skin, device, dtype)
+        lr = _build_graph(structures, rc_long + skin, device, dtype, g["pos64"])
         g["lr"] = {k: lr[k] for k in LR_KEYS}
     return g
 
 
-def _build_graph(structures, rc, device="cuda", dtype=torch.float32):
+def _build_graph(structures, rc, device="cuda", dtype=torch.float32, pos64=None):
     """CSR neighbour graph of a batch of structures, built on the GPU (see module docstring)."""
     items = [_as_struct(s) for s in structures]
     if not items:
@@ -123,8 +125,12 @@ def _build_graph(structures, rc, device="cuda", dtype=torch.float32):
     sizes = [len(it[1]) for it in items]
     offs = np.concatenate([[0], np.cumsum(sizes)])
     pos_np = np.concatenate([it[0] for it in items])
-    pos64 = torch.as_tensor(pos_np, dtype=torch.float64, device=dev).contiguous()
+    if pos64 is None:
+        pos64 = torch.as_tensor(pos_np, dtype=torch.float64, device=dev)
+    pos64 = pos64.contiguous()
     N = pos64.shape[0]
+    if tuple(pos64.shape) != (len(pos_np), 3) or pos64.dtype != torch.float64 or pos64.device.type != "cuda":
+        raise ValueError("pos64 must be the batch's (N, 3) float64 positions on the build device")
     pieces = []
     if not any(it[3] for it in items):
         sstart = torch.as_tensor(offs, dtype=torch.int32, device=dev)
@@ -141,19 +147,22 @@ def _build_graph(structures, rc, device="cuda", dtype=torch.float32):
                 aa = torch.zeros(sizes[k], dtype=torch.int32, device=dev)
                 rows = _molecule_rows(sub, ss, aa, rc, dtype)
             pieces.append((o, 0, *rows))
-    # concatenate rows in atom order with global indices
-    rps, eis, ejs, Ss, shs = [], [], [], [], []
-    e_off = 0
-    for o, _, rp, ei, ej, S, sh in pieces:
-        rps.append(rp[:-1] + e_off)
-        eis.append(ei + o)
-        ejs.append(ej + o)
-        Ss.append(S)
-        shs.append(sh)
-        e_off += int(rp[-1])
-    row_ptr = torch.cat(rps + [torch.tensor([e_off], dtype=torch.int64, device=dev)]).to(torch.int32)
-    ei, ej = torch.cat(eis).contiguous(), torch.cat(ejs).contiguous()
-    S, shift = torch.cat(Ss).contiguous(), torch.cat(shs).contiguous()
+    if len(pieces) == 1:                          # one piece (one structure, or the batched molecule rows)
+        _, _, rp, ei, ej, S, shift = pieces[0]
+        row_ptr = rp.to(torch.int32)
+    else:                                         # concatenate rows in atom order with global indices
+        rps, eis, ejs, Ss, shs = [], [], [], [], []
+        e_off = 0
+        for o, _, rp, ei, ej, S, sh in pieces:
+            rps.append(rp[:-1] + e_off)
+            eis.append(ei + o)
+            ejs.append(ej + o)
+            Ss.append(S)
+            shs.append(sh)
+            e_off += int(rp[-1])
+        row_ptr = torch.cat(rps + [torch.tensor([e_off], dtype=torch.int64, device=dev)]).to(torch.int32)
+        ei, ej = torch.cat(eis).contiguous(), torch.cat(ejs).contiguous()
+        S, shift = torch.cat(Ss).contiguous(), torch.cat(shs).contiguous()
     E = ei.numel()
     rev = torch.empty(E, dtype=torch.int32, device=dev)
     _lib.call("facek_nlist_reverse", _lib.ptr(row_ptr), _lib.ptr(ei), _lib.ptr(ej), _lib.ptr(S), N, E, _lib.ptr(rev),
@@ -161,7 +170,7 @@ def _build_graph(structures, rc, device="cuda", dtype=torch.float32):
     if E and bool((rev < 0).any()):
         raise RuntimeError("neighbour list is not symmetric (reverse edge missing)")
     cells = np.stack([it[2] if it[3] else np.zeros((3, 3)) for it in items])
-    return {"pos": torch.as_tensor(pos_np, dtype=dtype, device=dev), "pos64": pos64,
+    return {"pos": pos64.to(dtype, copy=True), "pos64": pos64,
             "meta": structure_meta(sizes, cells, dev),
             "Z": torch.as_tensor(np.concatenate([it[1] for it in items]), dtype=torch.long, device=dev),
             "batch": torch.as_tensor(np.repeat(np.arange(len(items)), sizes), dtype=torch.long, device=dev),
@@ -186,7 +195,7 @@ def periodic_graph_device(pos64, Z, cell, rc, dtype=torch.float32):
     rev = torch.empty(E, dtype=torch.int32, device=dev)
     _lib.call("facek_nlist_reverse", _lib.ptr(row_ptr), _lib.ptr(ei), _lib.ptr(ej), _lib.ptr(S), N, E, _lib.ptr(rev),
               _lib.stream())
-    return {"pos": pos64.to(dtype), "pos64": pos64, "meta": structure_meta([N], cell[None], dev), "Z": Z,
+    return {"pos": pos64.to(dtype, copy=True), "pos64": pos64, "meta": structure_meta([N], cell[None], dev), "Z": Z,
             "batch": torch.zeros(N, dtype=torch.long, device=dev), "nstr": 1,
             "natoms": torch.tensor([N], dtype=torch.long, device=dev),
             "cell": torch.as_tensor(cell[None], dtype=dtype, device=dev), "cell64": cell[None], "pbc": [True],
