@@ -173,7 +173,8 @@ def _build_graph(structures, rc, device="cuda", dtype=torch.float32, pos64=None)
     return {"pos": pos64.to(dtype, copy=True), "pos64": pos64,
             "meta": structure_meta(sizes, cells, dev),
             "Z": torch.as_tensor(np.concatenate([it[1] for it in items]), dtype=torch.long, device=dev),
-            "batch": torch.as_tensor(np.repeat(np.arange(len(items)), sizes), dtype=torch.long, device=dev),
+            "batch": (torch.zeros(N, dtype=torch.long, device=dev) if len(items) == 1 else
+                      torch.as_tensor(np.repeat(np.arange(len(items)), sizes), dtype=torch.long, device=dev)),
             "nstr": len(items), "natoms": torch.as_tensor(sizes, dtype=torch.long, device=dev),
             "cell": torch.as_tensor(cells, dtype=dtype, device=dev),
             "cell64": cells, "pbc": [it[3] for it in items],
