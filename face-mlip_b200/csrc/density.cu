@@ -56,7 +56,9 @@ __global__ void __launch_bounds__(256) dens_fwd_k(const T* __restrict__ phi, con
                                                   int B, int K) {
   extern __shared__ __align__(16) unsigned char smem_raw[];
   const int tile_elems = FWD_TILE * (NX + B + K);
-  T* buf[2] = {reinterpret_cast<T*>(smem_raw), reinterpret_cast<T*>(smem_raw) + tile_elems};
+  // the two tile buffers by offset (a pointer array indexed by the buffer number would live in local memory)
+  T* const buf0 = reinterpret_cast<T*>(smem_raw);
+  auto buf = [&](int c) { return buf0 + c * tile_elems; };
   const int nb = B / TB, nk = K / TK;
   const int tid = threadIdx.x, nthr = blockDim.x;
   const int tb = tid / nk, tk = tid - (tid / nk) * nk;
@@ -97,7 +99,7 @@ __global__ void __launch_bounds__(256) dens_fwd_k(const T* __restrict__ phi, con
   int64_t i = (int64_t)blockIdx.x - gridDim.x, e0 = 0;
   int t0 = 0, deg = 0;
   advance(i, t0, e0, deg);                      // first non-empty row (t0 = 0)
-  if (i < N) issue(buf[0], e0, t0, deg);
+  if (i < N) issue(buf(0), e0, t0, deg);
   T acc[TB][TK][NX];
 #pragma unroll
   for (int a = 0; a < TB; a++)
@@ -111,14 +113,14 @@ __global__ void __launch_bounds__(256) dens_fwd_k(const T* __restrict__ phi, con
     int nt0 = t0, ndeg = deg;
     advance(ni, nt0, ne0, ndeg);
     if (ni < N) {
-      issue(buf[cur ^ 1], ne0, nt0, ndeg);
+      issue(buf(cur ^ 1), ne0, nt0, ndeg);
       cp_async_wait<1>();
     } else {
       cp_async_wait<0>();
     }
     __syncthreads();
     const int nt = min(FWD_TILE, deg - t0);
-    const T* sY = buf[cur];
+    const T* sY = buf(cur);
     const T* sP = sY + FWD_TILE * NX;
     const T* sM = sP + FWD_TILE * B;
     if (active) {
