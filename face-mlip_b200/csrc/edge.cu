@@ -829,7 +829,7 @@ __global__ void __launch_bounds__(256) transport_bwd_k(const T* __restrict__ phi
 // and the pair adds its dphi and du halves with shuffles.  Same outputs as transport_bwd_k.  96 lanes = 48 edges
 // per round (rows with more edges loop).
 template <int BB>
-__global__ void __launch_bounds__(96, 5) transport_bwd_lane_k(const float* __restrict__ phi,
+__global__ void __launch_bounds__(96, 4) transport_bwd_lane_k(const float* __restrict__ phi,
                                                               const float* __restrict__ vec,
                                                               const int32_t* __restrict__ ej,
                                                               const float* __restrict__ Gt,
@@ -1180,7 +1180,7 @@ int transport_bwd(const void* phi, const void* vec, const int32_t* ej, const voi
     if (std::is_same<T, float>::value && B == 16 && Kd % 8 == 0 && 18 * 16 * Kd * 4 <= 48 * 1024) {
       // flagship shape: lane-per-edge kernel over the row's gradient rows in shared memory
       const size_t smem1 = sizeof(float) * 18 * 16 * (size_t)Kd;
-      transport_bwd_lane_k<16><<<grid_for(N, 5), 96, smem1, as_stream(stream)>>>(
+      transport_bwd_lane_k<16><<<grid_for(N, 4), 96, smem1, as_stream(stream)>>>(
           (const float*)phi, (const float*)vec, ej, (const float*)Gt, (const float*)dT1, (const float*)dT2, row_ptr,
           (float*)dphi, (float*)dvec, acc, (float*)dGe, N, Kd);
     } else if (B <= 16) {
