@@ -472,7 +472,7 @@ __global__ void __launch_bounds__(128) node_eng_fwd_k(const T* __restrict__ y0, 
 }
 
 template <typename T>
-__global__ void __launch_bounds__(128) node_eng_bwd_k(const T* __restrict__ y1, const T* __restrict__ y2,
+__global__ void __launch_bounds__(128, 4) node_eng_bwd_k(const T* __restrict__ y1, const T* __restrict__ y2,
                                                       const T* __restrict__ y3, const T* __restrict__ av,
                                                       const T* __restrict__ bv, const T* __restrict__ gI9,
                                                       const T* __restrict__ gV, const T* __restrict__ gMs,
