@@ -410,6 +410,32 @@ __global__ void radial_bwd_k(const T* __restrict__ vec, const T* __restrict__ dp
   }
 }
 
+// fp32, B/4 a power of two: B/4 consecutive lanes per edge, each a 16-byte piece of dphi and dphi/dr (a warp reads
+// contiguous 512-byte spans), the partial dot products joined by shuffles within the lane group.  Groups never
+// straddle a warp or the end of the range: the total E*B/4, the block size and the grid stride are all multiples of
+// the group size, so every lane a shuffle names is active.
+__global__ void radial_bwd4_k(const float* __restrict__ vec, const float4* __restrict__ dphi,
+                              const float4* __restrict__ dphidr, int B4, float* __restrict__ dvec, int acc,
+                              int64_t total) {
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const float4 a = __ldg(dphi + t), b = __ldg(dphidr + t);
+    float s = fmaf(a.w, b.w, fmaf(a.z, b.z, fmaf(a.y, b.y, a.x * b.x)));
+    const unsigned m = __activemask();
+    for (int o = 1; o < B4; o <<= 1) s += __shfl_xor_sync(m, s, o);
+    if ((t & (B4 - 1)) == 0) {
+      const int64_t e = t / B4;
+      const float vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+      const float r = sqrtf(vx * vx + vy * vy + vz * vz);
+      const float gx = s * vx / r, gy = s * vy / r, gz = s * vz / r;
+      if (acc) {
+        dvec[e * 3] += gx; dvec[e * 3 + 1] += gy; dvec[e * 3 + 2] += gz;
+      } else {
+        dvec[e * 3] = gx; dvec[e * 3 + 1] = gy; dvec[e * 3 + 2] = gz;
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------------------------------ messages
 template <typename T>
 __global__ void edge_msg_k(const T* __restrict__ Y, const int32_t* __restrict__ ei, const int32_t* __restrict__ ej,
@@ -1095,6 +1121,14 @@ template <typename T>
 int radial_bwd(const void* vec, const void* dphi, const void* dphidr, int B, void* dvec, int acc, int64_t E,
                void* stream) {
   if (E == 0) return FACEK_OK;
+  const int B4 = B / 4;
+  const uintptr_t al = reinterpret_cast<uintptr_t>(dphi) | reinterpret_cast<uintptr_t>(dphidr);
+  if (std::is_same<T, float>::value && B % 4 == 0 && B4 <= 32 && (B4 & (B4 - 1)) == 0 && (al & 15) == 0) {
+    const int64_t total = E * B4;
+    radial_bwd4_k<<<elem_grid(total, 256), 256, 0, as_stream(stream)>>>(
+        (const float*)vec, (const float4*)dphi, (const float4*)dphidr, B4, (float*)dvec, acc, total);
+    return launch_status("facek_radial_bwd");
+  }
   radial_bwd_k<T><<<elem_grid(E, 256), 256, 0, as_stream(stream)>>>((const T*)vec, (const T*)dphi,
                                                                      (const T*)dphidr, B, (T*)dvec, acc, E);
   return launch_status("facek_radial_bwd");
