@@ -80,6 +80,29 @@ __global__ void edge_sym_k(const T* __restrict__ vec, T* __restrict__ Y, int64_t
   }
 }
 
+// fp32: five lanes per edge, each storing one 16-byte piece (monomials 4q .. 4q+3) of the edge's 80-byte row, so a
+// warp's stores are contiguous (a thread per edge wrote 20 scalars at an 80-byte lane stride).  Each lane evaluates
+// all 20 monomials (a few dozen multiplies) and picks its piece with static indices.
+__global__ void edge_sym5_k(const float* __restrict__ vec, float4* __restrict__ Y, int64_t total) {
+  for (int64_t t = blockIdx.x * (int64_t)blockDim.x + threadIdx.x; t < total; t += (int64_t)gridDim.x * blockDim.x) {
+    const int64_t e = t / 5;
+    const int q = (int)(t - e * 5);
+    const float vx = vec[e * 3], vy = vec[e * 3 + 1], vz = vec[e * 3 + 2];
+    const float r = sqrtf(vx * vx + vy * vy + vz * vz);
+    float y[NX];
+    monomials(vx / r, vy / r, vz / r, y);
+    float4 o;
+    switch (q) {
+      case 0: o = make_float4(y[0], y[1], y[2], y[3]); break;
+      case 1: o = make_float4(y[4], y[5], y[6], y[7]); break;
+      case 2: o = make_float4(y[8], y[9], y[10], y[11]); break;
+      case 3: o = make_float4(y[12], y[13], y[14], y[15]); break;
+      default: o = make_float4(y[16], y[17], y[18], y[19]); break;
+    }
+    Y[t] = o;
+  }
+}
+
 template <typename T>
 __global__ void edge_sym_bwd_k(const T* __restrict__ vec, const T* __restrict__ dY, T* __restrict__ dvec, int acc,
                                int64_t E) {
@@ -1026,6 +1049,11 @@ int edge_vec_bwd(const void* dvec, const int32_t* row_ptr, const int32_t* rev, i
 template <typename T>
 int edge_sym(const void* vec, void* Y, int64_t E, void* stream) {
   if (E == 0) return FACEK_OK;
+  if (std::is_same<T, float>::value && (reinterpret_cast<uintptr_t>(Y) & 15) == 0) {
+    const int64_t total = E * 5;                        // NX = 20 floats = five 16-byte pieces per edge
+    edge_sym5_k<<<elem_grid(total, 256), 256, 0, as_stream(stream)>>>((const float*)vec, (float4*)Y, total);
+    return launch_status("facek_edge_sym");
+  }
   edge_sym_k<T><<<elem_grid(E, 256), 256, 0, as_stream(stream)>>>((const T*)vec, (T*)Y, E);
   return launch_status("facek_edge_sym");
 }
